@@ -1,0 +1,328 @@
+"""Benchmark: LTC fwd+bwd throughput (B*T/s) of the sm_100a solver, 1..8 GPUs.
+
+Default workload: configuration c3 (B=4096 batch-sharded over the ranks, T=128,
+D=128, H=64, ode_unfolds=6, density 0.5/0.5): one training step = module forward
+(LayerNorm, affine, softplus transforms, solver), sum loss, backward, gradient
+all-reduce (SUM, NCCL, when N>1) and an Adam step.  Other configurations
+(--config c0..c4) run forward+backward with the same harness.
+
+  python bench.py [--gpus N --steps K --warmup W --config c3]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+  python bench.py --impl reference     # reference CPU path (oracle port) on host cores
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "ltc-cuda_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import synth  # noqa: E402
+
+METRIC = "fwd+bwd sequence-timesteps/sec (B·T/s) at 1/2/4/8 B200; % FP32 roofline"
+UNIT = "B*T/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c3", choices=sorted(synth.CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "sm_max_mhz": 1965.0}, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this rank's GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# --------------------------------------------------------------------------- CPU arm
+def cpu_sample_rate(cfg, seconds: float, threads: int):
+    """Oracle port (restatement of the reference TorchScript path) timed on host cores:
+    module-level fwd+bwd with sum loss on a bounded batch/time slice of the workload."""
+    from oracle import ltc_oracle as orc
+    torch.set_num_threads(threads)
+    Bs = {"c0": 24, "c1": 16, "c2": 8, "c3": 64, "c4": 1}[cfg.name]
+    Ts = {"c0": 8, "c1": 32, "c2": 8, "c3": 8, "c4": 2}[cfg.name]
+    p, x = synth.make_workload(cfg, batch=Bs)
+    x = x[:, :Ts].contiguous()
+    params = {k: v.clone().requires_grad_(k in orc.parameter_names()) for k, v in p.items()}
+
+    def one():
+        out, _ = orc.module_forward(params, x, None, cfg.dt, cfg.U)
+        out.sum().backward()
+        for v in params.values():
+            v.grad = None
+
+    one()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        one()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 1000:
+            break
+    return {"value": n * Bs * Ts / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{cfg.name} slice B={Bs} T={Ts} (D={cfg.D} H={cfg.H} U={cfg.U}), module fwd+bwd sum loss, "
+                      f"{n} reps in {el:.1f}s, oracle restatement of the reference TorchScript path"}
+
+
+def run_reference(args, cfg, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    from oracle import ltc_oracle as orc
+    torch.set_num_threads(threads)
+    Bs, Ts = {"c0": (24, 8), "c1": (16, 32), "c2": (8, 8), "c3": (256, 8), "c4": (1, 2)}[cfg.name]
+    p, x = synth.make_workload(cfg, batch=Bs)
+    x = x[:, :Ts].contiguous()
+    params = {k: v.clone().requires_grad_(k in orc.parameter_names()) for k, v in p.items()}
+
+    def step():
+        out, _ = orc.module_forward(params, x, None, cfg.dt, cfg.U)
+        out.sum().backward()
+        for v in params.values():
+            v.grad = None
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = args.steps * Bs * Ts / el
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": cfg.name, "B": Bs, "T": Ts, "D": cfg.D, "H": cfg.H, "U": cfg.U,
+                       "sample_of": {"B": cfg.B, "T": cfg.T}},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{cfg.name} slice B={Bs} T={Ts} per step; CPU restatement of the "
+                                       "reference TorchScript solver (module fwd+bwd, sum loss)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    cfg = synth.CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+
+    import ltc_cuda
+    import ltc_layer
+    from data_parallel import FlatGradBucket, shard_range, training_step
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    peaks, peaks_kind = measured_peaks()
+
+    p, x_full = synth.make_workload(cfg)
+    lo, hi = shard_range(cfg.B, rank, world)
+    Bl = hi - lo
+    model = ltc_layer.TrueLiquidTimeConstant(cfg.D, cfg.H, dt=cfg.dt, ode_unfolds=cfg.U,
+                                             sparsity=cfg.density, sensory_sparsity=cfg.sensory_density)
+    model.load_state_dict(p)
+    model = model.to(dev)
+    bucket = FlatGradBucket(model.parameters())
+    opt = torch.optim.Adam(model.parameters(), lr=1e-4, fused=True)
+    x_host = x_full[lo:hi].contiguous().pin_memory()
+    x_dev = x_host.to(dev)
+    del x_full
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def step(x):
+        if cfg.training_step:
+            return training_step(model, x, bucket, opt)
+        bucket.zero()
+        out, _ = model(x)
+        loss = out.sum()
+        loss.backward()
+        bucket.all_reduce()
+        return loss.detach()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, args.warmup)):
+        step(x_dev)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region ----
+    clocks = ClockSampler(physical_gpu_index(local))
+    clocks.start()
+    ltc_cuda.timing_enable(True)
+    n0 = ltc_cuda.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        flush.zero_()
+        step(x_dev)
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = ltc_cuda.launch_count() - n0
+    ktimes = ltc_cuda.timing_collect()
+    ltc_cuda.timing_enable(False)
+    clk = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    value = cfg.B * cfg.T / (ms / 1e3)
+
+    # ---- end to end through the public API: pinned host input -> device, loss -> host ----
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        flush.zero_()
+        xd = x_host.to(dev, non_blocking=True)
+        loss = step(xd)
+        float(loss.item())
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    e2e = {"value": cfg.B * cfg.T / (ms_e2e / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
+           "d2h_bytes_per_step": 4 * world, "ms_per_step": ms_e2e}
+
+    # ---- roofline of the dominant kernel (MUFU pipe: 2 MUFU ops per synapse visit) ----
+    f_mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    visits = {"recurrent_fwd": Bl * cfg.T * cfg.U * cfg.H * cfg.H,
+              "recurrent_bwd": Bl * cfg.T * cfg.U * cfg.H * cfg.H,
+              "sensory_fwd": Bl * cfg.T * cfg.D * cfg.H,
+              "sensory_bwd": Bl * cfg.T * cfg.D * cfg.H}
+    dom = max(visits, key=lambda k: ktimes[k][0])
+    tot_ms, n_l = ktimes[dom]
+    per_launch_s = tot_ms / max(1, n_l) / 1e3
+    achieved = visits[dom] / per_launch_s / 1e9
+    peak = sms * 16 / 2 * f_mhz * 1e6 / 1e9  # Gvisits/s: 16 MUFU/clk/SM, 2 MUFU per visit
+    kernels = {k: {"ms_total": round(v[0], 3), "launches": v[1], "share": round(v[0] / max(1e-9, sum(
+        t for t, _ in ktimes.values())), 4)} for k, v in ktimes.items()}
+    # whole-step ceiling with the survey's counting convention (4 MUFU per fwd+bwd synapse visit)
+    S = cfg.D * cfg.H + cfg.U * cfg.H * cfg.H
+    t_roof = cfg.B * cfg.T * S * 4 / (16 * sms * f_mhz * 1e6 * world)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; distributions of the config)",
+        "config": {"workload": cfg.name, "B": cfg.B, "T": cfg.T, "D": cfg.D, "H": cfg.H, "U": cfg.U,
+                   "density": cfg.density, "sensory_density": cfg.sensory_density,
+                   "step": "train (fwd+bwd+allreduce+adam)" if cfg.training_step else "fwd+bwd",
+                   "parallelism": f"dp{world}", "per_rank_batch": Bl,
+                   "l2": "256 MB flush write between steps (inside the timed region)"},
+        "e2e": e2e,
+        "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_basis": f"{sms} SMs x 16 MUFU/clk / 2 MUFU per visit at sm_max {f_mhz:.0f} MHz ({peaks_kind})",
+                     "step_frac_survey_convention": t_roof / (ms / 1e3)},
+        "kernels": kernels,
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample_rate(cfg, args.cpu_seconds, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

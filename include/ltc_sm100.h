@@ -1,0 +1,140 @@
+/*
+ * ltc_sm100.h -- C-ABI of the B200 (sm_100a) LTC ODE-solver library (libltc_sm100.so).
+ *
+ * The library replaces the reference's compiled solver, the pybind11 module
+ * built from csrc/ltc_kernels.cu (bindings at csrc/ltc_kernels.cu:1307-1314),
+ * which ltc_cuda.py loads and calls from LTCCudaForward (ltc_cuda.py:241-359).
+ * All pointers are DEVICE pointers to contiguous fp32 arrays unless stated;
+ * every call is asynchronous on the given stream and allocates nothing: the
+ * caller provides the output, saved-state and workspace buffers whose sizes
+ * ltc_plan() reports.  Status 0 = success; non-zero = error, described by
+ * ltc_last_error() (per calling thread).
+ *
+ * Layouts:  x (B,T,D); state (B,H); outputs (B,T,H);
+ *           recurrent matrices (H,H) indexed [presynaptic, postsynaptic];
+ *           sensory matrices (D,H) indexed [input, postsynaptic]; vectors (H).
+ */
+#ifndef LTC_SM100_H
+#define LTC_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ltc_stream_t; /* == cudaStream_t */
+
+/* Problem size.  ode_unfolds and epsilon mean what they mean in
+ * ltc_full_forward (csrc/ltc_kernels.cu:1179-1181). */
+typedef struct {
+  int32_t B, T, D, H;
+  int32_t ode_unfolds;
+  float epsilon;
+  int32_t flags; /* LTC_FLAG_* */
+} LtcDims;
+
+#define LTC_FLAG_FORCE_WIDE 1 /* use the streamed wide-H kernels even for H <= 64 */
+
+/* The 11 parameter inputs of ltc_full_forward (csrc/ltc_kernels.cu:1167-1178),
+ * untransposed, in the same order. */
+typedef struct {
+  const float* w_pos;         /* (H,H) softplus(w) * mask            */
+  const float* w_erev;        /* (H,H) w_pos * erev                  */
+  const float* mu;            /* (H,H)                               */
+  const float* sigma;         /* (H,H)                               */
+  const float* sensory_mu;    /* (D,H)                               */
+  const float* sensory_sigma; /* (D,H)                               */
+  const float* sensory_erev;  /* (D,H)                               */
+  const float* sensory_w_pos; /* (D,H) softplus(sensory_w) * mask    */
+  const float* cm_t;          /* (H)   softplus(cm) / (dt / unfolds) */
+  const float* gleak_pos;     /* (H)                                 */
+  const float* vleak;         /* (H)                                 */
+} LtcParams;
+
+/* The 13 gradient outputs of ltc_full_backward (csrc/ltc_kernels.cu:1139-1153 and
+ * ltc_cuda.py:342-355), in the same order.  Every pointer must be valid. */
+typedef struct {
+  float* x_seq;          /* (B,T,D) */
+  float* state;          /* (B,H)   */
+  float* w_pos;          /* (H,H)   */
+  float* w_erev;         /* (H,H)   */
+  float* mu;             /* (H,H)   */
+  float* sigma;          /* (H,H)   */
+  float* sensory_mu;     /* (D,H)   */
+  float* sensory_sigma;  /* (D,H)   */
+  float* sensory_erev;   /* (D,H)   */
+  float* sensory_w_pos;  /* (D,H)   */
+  float* cm_t;           /* (H)     */
+  float* gleak_pos;      /* (H)     */
+  float* vleak;          /* (H)     */
+} LtcGrads;
+
+/* Buffer sizes (bytes) for a problem on the CURRENT device.  saved_bytes is the
+ * forward state kept for the backward pass (replaces v_buffers_stacked and the
+ * sensory stacks of ltc_full_forward, csrc/ltc_kernels.cu:1205-1212). */
+typedef struct {
+  size_t saved_bytes;
+  size_t fwd_workspace_bytes;
+  size_t bwd_workspace_bytes;
+  int32_t wide;       /* 1 if the wide-H kernels will run */
+  int32_t padded_h;   /* neuron count the kernels pad H to */
+  int32_t fwd_ctas, bwd_ctas;
+} LtcPlan;
+
+int ltc_plan(const LtcDims* dims, LtcPlan* out);
+
+/* Forward solve over all T steps (replaces ltc_full_forward,
+ * csrc/ltc_kernels.cu:1165-1300).  h0 may be NULL (zero state).  saved may be
+ * NULL when no backward pass follows (save_intermediates = false); otherwise it
+ * must hold plan.saved_bytes. */
+int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, const float* h0,
+                float* outputs, float* h_final, void* saved, void* workspace, size_t workspace_bytes,
+                ltc_stream_t stream);
+
+/* Backward pass over all T steps (replaces ltc_full_backward,
+ * csrc/ltc_kernels.cu:962-1154).  grad_outputs is addressed with the element
+ * strides go_strides[3] (B,T,H order; stride 0 allowed, e.g. from out.sum()).
+ * grad_state may be NULL (no gradient on the returned state).  Deterministic:
+ * no atomics; fixed-order reductions. */
+int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, const void* saved,
+                 const float* grad_outputs, const int64_t go_strides[3], const float* grad_state,
+                 const LtcGrads* grads, void* workspace, size_t workspace_bytes, ltc_stream_t stream);
+
+/* Kernel identifiers of the launches each call issues (forward: PACK_FWD,
+ * SENSORY_FWD, RECURRENT_FWD; backward: PACK_BWD, RECURRENT_BWD, SENSORY_BWD, FINISH). */
+enum {
+  LTC_KERNEL_PACK_FWD = 0,
+  LTC_KERNEL_SENSORY_FWD = 1,
+  LTC_KERNEL_RECURRENT_FWD = 2,
+  LTC_KERNEL_PACK_BWD = 3,
+  LTC_KERNEL_RECURRENT_BWD = 4,
+  LTC_KERNEL_SENSORY_BWD = 5,
+  LTC_KERNEL_FINISH = 6,
+  LTC_NUM_KERNELS = 7
+};
+
+/* Per-launch device timing, process-wide (no counterpart in the
+ * reference, whose bench times with torch.profiler, bench_ltc.py:292-387).
+ * While enabled, every launch is bracketed by a cudaEvent pair recorded on its
+ * own stream.  ltc_timing_collect() waits for them, writes the summed
+ * milliseconds and launch counts per LTC_KERNEL_* id (n >= LTC_NUM_KERNELS) and
+ * clears the record. */
+int ltc_timing_enable(int on);
+int ltc_timing_collect(double* total_ms, int32_t* launches, int n);
+
+/* Number of kernels launched through the library by this process. */
+int64_t ltc_launch_count(void);
+
+/* Last error message of the calling thread ("" if none). */
+const char* ltc_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ltc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTC_SM100_H */

@@ -1,0 +1,393 @@
+// extern "C" entry points of libltc_sm100.so (declared in include/ltc_sm100.h).
+//
+// Host-side orchestration is three (forward) / four (backward) launches on the
+// caller's stream, independent of T and ode_unfolds:
+//   forward : pack -> sensory_fwd (all B*T rows) -> recurrent_fwd (all T*U unfolds)
+//   backward: pack -> recurrent_bwd -> sensory_bwd -> finish (reductions + transforms)
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ltc_sm100.h"
+#include "ltc_internal.h"
+
+using namespace ltc;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return 1;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail("%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Optional per-launch timing (ltc_timing_enable): a cudaEvent pair recorded on
+// the launch stream around every kernel; ltc_timing_collect() sums them.
+struct Timing {
+  bool on = false;
+  std::vector<cudaEvent_t> start, stop;
+  std::vector<int> kid;
+  size_t used = 0;
+  long long launches = 0;
+};
+Timing g_tm;           // process-wide: the backward pass runs on autograd's worker thread
+std::mutex g_tm_mu;
+
+class TimedLaunch {
+ public:
+  TimedLaunch(int kid, cudaStream_t st) : st_(st), idx_(-1) {
+    std::lock_guard<std::mutex> lk(g_tm_mu);
+    ++g_tm.launches;
+    if (!g_tm.on) return;
+    if (g_tm.used == g_tm.start.size()) {
+      cudaEvent_t a, b;
+      if (cudaEventCreate(&a) != cudaSuccess) return;
+      if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return; }
+      g_tm.start.push_back(a);
+      g_tm.stop.push_back(b);
+      g_tm.kid.push_back(kid);
+    }
+    idx_ = (long long)g_tm.used++;
+    g_tm.kid[idx_] = kid;
+    cudaEventRecord(g_tm.start[idx_], st_);
+  }
+  ~TimedLaunch() {
+    if (idx_ < 0) return;
+    std::lock_guard<std::mutex> lk(g_tm_mu);
+    cudaEventRecord(g_tm.stop[idx_], st_);
+  }
+
+ private:
+  cudaStream_t st_;
+  long long idx_;
+};
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+};
+
+DeviceInfo device_info(int* err) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = cuda_fail(e == cudaSuccess ? cudaErrorInvalidDevice : e, "cudaGetDevice");
+    return DeviceInfo{};
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev].sms == 0) {
+    int sms = 0, major = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess) {
+      *err = cuda_fail(e, "cudaDeviceGetAttribute");
+      return DeviceInfo{};
+    }
+    cache[dev].sms = sms;
+    cache[dev].major = major;
+  }
+  *err = 0;
+  return cache[dev];
+}
+
+// Carves 256-byte aligned sub-buffers out of one caller-provided allocation.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+struct Layout {
+  RecPlan rp;
+  SensBwdPlan sp;
+  long long rows;
+  size_t saved_floats_v, saved_floats_r;
+};
+
+int check_dims(const LtcDims* d) {
+  if (!d) return fail("dims is NULL");
+  if (d->B < 1 || d->T < 1 || d->D < 1 || d->H < 1 || d->ode_unfolds < 1)
+    return fail("invalid dims: B=%d T=%d D=%d H=%d ode_unfolds=%d (all must be >= 1)", d->B, d->T, d->D,
+                d->H, d->ode_unfolds);
+  if (d->H > 512) return fail("H=%d exceeds the supported maximum of 512", d->H);
+  return 0;
+}
+
+int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
+  if (check_dims(d)) return 1;
+  int err = 0;
+  *di = device_info(&err);
+  if (err) return 1;
+  if (di->major != 10)
+    return fail("libltc_sm100 requires an sm_100 (B200-class) GPU; current device is compute capability %d.x",
+                di->major);
+  L->rp = plan_recurrent(d->B, d->H, di->sms, d->flags & LTC_FLAG_FORCE_WIDE);
+  L->rows = (long long)d->B * d->T;
+  L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
+  const size_t tu = (size_t)d->T * d->ode_unfolds;
+  L->saved_floats_v = (tu + 1) * d->B * d->H;
+  L->saved_floats_r = tu * d->B * d->H;
+  return 0;
+}
+
+struct FwdBuffers {
+  float4 *pack, *spack, *nrn;
+  float *sn, *sd;
+};
+size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
+  Carver c(ws);
+  const int HP = L.rp.HP;
+  b->pack = c.take<float4>((size_t)HP * HP);
+  b->spack = c.take<float4>((size_t)d->D * HP);
+  b->nrn = c.take<float4>(HP);
+  b->sn = c.take<float>((size_t)L.rows * d->H);
+  b->sd = c.take<float>((size_t)L.rows * d->H);
+  return c.off + 256;
+}
+
+struct BwdBuffers {
+  float4 *pack, *packT, *spack, *nrn;
+  float *gsn, *gsd, *rpart, *rpartn, *spart, *dxpart;
+};
+size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
+  Carver c(ws);
+  const int HP = L.rp.HP;
+  b->pack = c.take<float4>((size_t)HP * HP);
+  b->packT = c.take<float4>((size_t)HP * HP);
+  b->spack = c.take<float4>((size_t)d->D * HP);
+  b->nrn = c.take<float4>(HP);
+  b->gsn = c.take<float>((size_t)L.rows * d->H);
+  b->gsd = c.take<float>((size_t)L.rows * d->H);
+  b->rpart = c.take<float>((size_t)L.rp.slots_bwd * 4 * HP * HP);
+  b->rpartn = c.take<float>((size_t)L.rp.slots_bwd * 3 * HP);
+  b->spart = c.take<float>(L.sp.part_floats);
+  b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
+  return c.off + 256;
+}
+
+PackArgs pack_args(const LtcDims* d, const LtcParams* p, int HP) {
+  PackArgs a{};
+  a.w_pos = p->w_pos; a.w_erev = p->w_erev; a.mu = p->mu; a.sigma = p->sigma;
+  a.smu = p->sensory_mu; a.ssig = p->sensory_sigma; a.serev = p->sensory_erev; a.sw = p->sensory_w_pos;
+  a.cm = p->cm_t; a.gl = p->gleak_pos; a.vl = p->vleak;
+  a.D = d->D; a.H = d->H; a.HP = HP;
+  return a;
+}
+
+int check_params(const LtcParams* p) {
+  if (!p) return fail("params is NULL");
+  const void* ptrs[] = {p->w_pos, p->w_erev, p->mu, p->sigma, p->sensory_mu, p->sensory_sigma,
+                        p->sensory_erev, p->sensory_w_pos, p->cm_t, p->gleak_pos, p->vleak};
+  for (const void* q : ptrs)
+    if (!q) return fail("a parameter pointer is NULL");
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ltc_last_error(void) { return g_last_error.c_str(); }
+
+int ltc_version(void) { return 100; }
+
+int ltc_timing_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_tm_mu);
+  g_tm.on = on != 0;
+  g_tm.used = 0;
+  return 0;
+}
+
+int ltc_timing_collect(double* total_ms, int32_t* launches, int n) {
+  if (!total_ms || !launches || n < LTC_NUM_KERNELS) return fail("ltc_timing_collect: need %d slots", LTC_NUM_KERNELS);
+  std::lock_guard<std::mutex> lk(g_tm_mu);
+  for (int k = 0; k < n; ++k) {
+    total_ms[k] = 0.0;
+    launches[k] = 0;
+  }
+  for (size_t i = 0; i < g_tm.used; ++i) {
+    cudaError_t e = cudaEventSynchronize(g_tm.stop[i]);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize");
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, g_tm.start[i], g_tm.stop[i]);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime");
+    total_ms[g_tm.kid[i]] += ms;
+    launches[g_tm.kid[i]] += 1;
+  }
+  g_tm.used = 0;
+  return 0;
+}
+
+int64_t ltc_launch_count(void) {
+  std::lock_guard<std::mutex> lk(g_tm_mu);
+  return g_tm.launches;
+}
+
+int ltc_plan(const LtcDims* dims, LtcPlan* out) {
+  Layout L;
+  DeviceInfo di;
+  if (!out) return fail("out is NULL");
+  if (make_layout(dims, &L, &di)) return 1;
+  FwdBuffers fb;
+  BwdBuffers bb;
+  out->saved_bytes = (L.saved_floats_v + L.saved_floats_r) * sizeof(float) + 256;
+  out->fwd_workspace_bytes = carve_fwd(dims, L, nullptr, &fb);
+  out->bwd_workspace_bytes = carve_bwd(dims, L, nullptr, &bb);
+  out->wide = L.rp.wide ? 1 : 0;
+  out->padded_h = L.rp.HP;
+  out->fwd_ctas = L.rp.grid_fwd;
+  out->bwd_ctas = L.rp.grid_bwd;
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, const float* h0, float* outputs,
+                float* h_final, void* saved, void* workspace, size_t workspace_bytes, ltc_stream_t stream) {
+  Layout L;
+  DeviceInfo di;
+  if (make_layout(dims, &L, &di) || check_params(params)) return 1;
+  if (!x || !outputs || !h_final || !workspace) return fail("ltc_forward: NULL x/outputs/h_final/workspace");
+  FwdBuffers b;
+  const size_t need = carve_fwd(dims, L, nullptr, &b);
+  if (workspace_bytes < need)
+    return fail("ltc_forward: workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                need);
+  carve_fwd(dims, L, workspace, &b);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int HP = L.rp.HP;
+
+  PackArgs pa = pack_args(dims, params, HP);
+  pa.pack = b.pack; pa.packT = nullptr; pa.spack = b.spack; pa.nrn = b.nrn;
+  cudaError_t e;
+  {
+    TimedLaunch tl(LTC_KERNEL_PACK_FWD, st);
+    e = launch_pack(pa, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "pack");
+
+  SensFwdArgs sa{};
+  sa.spack = b.spack; sa.x = x; sa.sn = b.sn; sa.sd = b.sd; sa.rows = L.rows;
+  sa.D = dims->D; sa.H = dims->H; sa.HP = HP;
+  {
+    TimedLaunch tl(LTC_KERNEL_SENSORY_FWD, st);
+    e = launch_sensory_fwd(sa, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "sensory_fwd");
+
+  RecFwdArgs ra{};
+  ra.pack = b.pack; ra.nrn = b.nrn; ra.sn = b.sn; ra.sd = b.sd; ra.h0 = h0;
+  ra.out = outputs; ra.hT = h_final;
+  if (saved) {
+    Carver c(saved);
+    ra.V = c.take<float>(L.saved_floats_v);
+    ra.R = c.take<float>(L.saved_floats_r);
+  }
+  ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
+  ra.ns = L.rp.ns_fwd; ra.eps = dims->epsilon;
+  {
+    TimedLaunch tl(LTC_KERNEL_RECURRENT_FWD, st);
+    e = launch_recurrent_fwd(ra, L.rp, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "recurrent_fwd");
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, const void* saved,
+                 const float* grad_outputs, const int64_t go_strides[3], const float* grad_state,
+                 const LtcGrads* grads, void* workspace, size_t workspace_bytes, ltc_stream_t stream) {
+  Layout L;
+  DeviceInfo di;
+  if (make_layout(dims, &L, &di) || check_params(params)) return 1;
+  if (!x || !saved || !grad_outputs || !go_strides || !grads || !workspace)
+    return fail("ltc_backward: NULL x/saved/grad_outputs/go_strides/grads/workspace");
+  const float* gp[] = {grads->x_seq, grads->state, grads->w_pos, grads->w_erev, grads->mu, grads->sigma,
+                       grads->sensory_mu, grads->sensory_sigma, grads->sensory_erev, grads->sensory_w_pos,
+                       grads->cm_t, grads->gleak_pos, grads->vleak};
+  for (const float* q : gp)
+    if (!q) return fail("ltc_backward: a gradient output pointer is NULL");
+  BwdBuffers b;
+  const size_t need = carve_bwd(dims, L, nullptr, &b);
+  if (workspace_bytes < need)
+    return fail("ltc_backward: workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                need);
+  carve_bwd(dims, L, workspace, &b);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int HP = L.rp.HP;
+
+  PackArgs pa = pack_args(dims, params, HP);
+  pa.pack = b.pack; pa.packT = b.packT; pa.spack = b.spack; pa.nrn = b.nrn;
+  cudaError_t e;
+  {
+    TimedLaunch tl(LTC_KERNEL_PACK_BWD, st);
+    e = launch_pack(pa, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "pack");
+
+  Carver sc(const_cast<void*>(saved));
+  RecBwdArgs ra{};
+  ra.pack = b.pack; ra.packT = b.packT; ra.nrn = b.nrn;
+  ra.V = sc.take<float>(L.saved_floats_v);
+  ra.R = sc.take<float>(L.saved_floats_r);
+  ra.gout = grad_outputs; ra.go_sb = go_strides[0]; ra.go_st = go_strides[1]; ra.go_sh = go_strides[2];
+  ra.gstate = grad_state; ra.gsn = b.gsn; ra.gsd = b.gsd; ra.gh0 = grads->state;
+  ra.part = b.rpart; ra.partn = b.rpartn;
+  ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
+  ra.ns = L.rp.ns_bwd;
+  {
+    TimedLaunch tl(LTC_KERNEL_RECURRENT_BWD, st);
+    e = launch_recurrent_bwd(ra, L.rp, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "recurrent_bwd");
+
+  SensBwdArgs sa{};
+  sa.spack = b.spack; sa.x = x; sa.gsn = b.gsn; sa.gsd = b.gsd; sa.dx = grads->x_seq;
+  sa.part = b.spart; sa.rows = L.rows; sa.D = dims->D; sa.H = dims->H; sa.HP = HP; sa.nsplit = L.sp.nsplit;
+  {
+    TimedLaunch tl(LTC_KERNEL_SENSORY_BWD, st);
+    e = launch_sensory_bwd(sa, L.sp, b.dxpart, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "sensory_bwd");
+
+  FinishArgs fa{};
+  fa.rec_part = b.rpart; fa.rec_partn = b.rpartn; fa.rslots = L.rp.slots_bwd; fa.rec_transposed = L.rp.wide;
+  fa.sens_part = b.spart; fa.nsplit = L.sp.nsplit; fa.dxpart = b.dxpart; fa.nqc = L.sp.nqc; fa.rows = L.rows;
+  fa.mu = params->mu; fa.sigma = params->sigma; fa.smu = params->sensory_mu; fa.ssig = params->sensory_sigma;
+  fa.serev = params->sensory_erev; fa.sw = params->sensory_w_pos;
+  fa.g_w_pos = grads->w_pos; fa.g_w_erev = grads->w_erev; fa.g_mu = grads->mu; fa.g_sigma = grads->sigma;
+  fa.g_smu = grads->sensory_mu; fa.g_ssig = grads->sensory_sigma; fa.g_serev = grads->sensory_erev;
+  fa.g_sw = grads->sensory_w_pos; fa.g_cm = grads->cm_t; fa.g_gl = grads->gleak_pos; fa.g_vl = grads->vleak;
+  fa.g_x = grads->x_seq; fa.D = dims->D; fa.H = dims->H; fa.HP = HP;
+  {
+    TimedLaunch tl(LTC_KERNEL_FINISH, st);
+    e = launch_finish(fa, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "finish");
+  g_last_error.clear();
+  return 0;
+}
+
+}  // extern "C"

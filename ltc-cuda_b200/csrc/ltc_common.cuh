@@ -1,0 +1,128 @@
+// Shared device helpers for the LTC solver kernels (sm_100a).
+//
+// Conventions used by every kernel in this library
+// ------------------------------------------------
+// * fp32 everywhere.  Recurrent matrices are (H, H) row-major indexed
+//   [pre p, post q]; sensory matrices are (D, H) indexed [input d, post q].
+// * A sigmoid gate  act = 1 / (1 + exp(-sigma * (v - mu)))  is evaluated as
+//   act = rcp(1 + ex2(y)),  y = sl * v + nm,  with the per-synapse constants
+//   sl = -sigma * log2(e) and nm = sigma * mu * log2(e) precomputed once
+//   ("gate pack").  ex2/rcp are the hardware MUFU approximations (ex2.approx,
+//   rcp.approx), each within 2 ulp, far inside the parity tolerances.
+// * Saved forward state for the backward pass:
+//     V[n][b][h], n = t*U + k, n in [0, T*U]: the input of unfold k at step t
+//       (V[T*U] is the final state);
+//     R[n][b][h], n in [0, T*U): 1 / (cm_t + gleak + den + eps) of that unfold.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define LTC_LOG2E 1.4426950408889634f
+#define LTC_LN2 0.6931471805599453f
+
+namespace ltc {
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// act = sigmoid(sigma * (v - mu)) given the gate pack (sl, nm).
+__device__ __forceinline__ float gate(float sl, float nm, float v) {
+  return rcp_approx(1.0f + ex2_approx(fmaf(sl, v, nm)));
+}
+
+// ---------------------------------------------------------------------------
+// Transposed reduction across the TPC lanes that share one neuron.
+//
+// Each of the TPC lanes (contiguous lanes, TPC a power of two <= 32) holds SB
+// partial sums, one per sample of a block.  Recursive halving exchanges half of
+// the remaining samples per step, so that after log2(min(SB,TPC)) exchanges
+// every lane holds full sums for SB/TPC samples (or, when TPC > SB, the
+// remaining steps are butterflies and TPC/SB lanes hold the same sample).
+// Fixed order => bitwise deterministic.
+//   NV  : number of independent value arrays reduced with the same pattern
+//   out : x[v][0 .. OWN-1] hold the sums for samples own_base() + i
+// ---------------------------------------------------------------------------
+template <int TPC, int SB>
+struct LaneReduce {
+  static constexpr int OWN = (SB >= TPC) ? SB / TPC : 1;
+
+  template <int NV>
+  __device__ __forceinline__ static void run(float (&x)[NV][SB], int lane) {
+    int count = SB;
+#pragma unroll
+    for (int stride = TPC / 2; stride >= 1; stride >>= 1) {
+      const bool hi = (lane & stride) != 0;
+      if (count > 1) {
+        const int half = count / 2;
+#pragma unroll
+        for (int k = 0; k < SB / 2; ++k) {
+          if (k < half) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+              const float send = hi ? x[v][k] : x[v][k + half];
+              const float keep = hi ? x[v][k + half] : x[v][k];
+              x[v][k] = keep + __shfl_xor_sync(0xffffffffu, send, stride);
+            }
+          }
+        }
+        count = half;
+      } else {
+#pragma unroll
+        for (int v = 0; v < NV; ++v) x[v][0] += __shfl_xor_sync(0xffffffffu, x[v][0], stride);
+      }
+    }
+  }
+
+  // first sample index (within the block) whose sums this lane holds
+  __device__ __forceinline__ static int own_base(int lane) {
+    int base = 0, count = SB;
+#pragma unroll
+    for (int stride = TPC / 2; stride >= 1; stride >>= 1) {
+      if (count > 1) {
+        const int half = count / 2;
+        if (lane & stride) base += half;
+        count = half;
+      }
+    }
+    return base;
+  }
+
+  // true for exactly one lane among those holding identical sums
+  __device__ __forceinline__ static bool writer(int lane) {
+    int count = SB;
+    bool w = true;
+#pragma unroll
+    for (int stride = TPC / 2; stride >= 1; stride >>= 1) {
+      if (count > 1) {
+        count /= 2;
+      } else if (lane & stride) {
+        w = false;
+      }
+    }
+    return w;
+  }
+};
+
+// 4-byte asynchronous global->shared copy (Ampere+ cp.async, valid on sm_100a)
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::); }
+
+}  // namespace ltc

@@ -1,0 +1,137 @@
+// Internal launch interfaces shared by the kernel translation units and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ltc {
+
+// ---- parameter packing --------------------------------------------------
+struct PackArgs {
+  const float* w_pos;   // (H,H)
+  const float* w_erev;  // (H,H)
+  const float* mu;      // (H,H)
+  const float* sigma;   // (H,H)
+  const float* smu;     // (D,H)
+  const float* ssig;    // (D,H)
+  const float* serev;   // (D,H)
+  const float* sw;      // (D,H)
+  const float* cm;      // (H)
+  const float* gl;      // (H)
+  const float* vl;      // (H)
+  float4* pack;         // [HP][HP]  (sl, nm, w_pos, w_erev) indexed [p][q]
+  float4* packT;        // [HP][HP]  same, indexed [q][p]   (may be null)
+  float4* spack;        // [D][HP]   (sl, nm, sw, sw*serev)
+  float4* nrn;          // [HP]      (cm, gl, vl, gl*vl)
+  int D, H, HP;
+};
+cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);
+
+// ---- sensory forward: sn/sd per row (row = b*T + t) ----------------------
+struct SensFwdArgs {
+  const float4* spack;  // [D][HP]
+  const float* x;       // (rows, D)
+  float* sn;            // (rows, H)
+  float* sd;            // (rows, H)
+  long long rows;
+  int D, H, HP;
+};
+cudaError_t launch_sensory_fwd(const SensFwdArgs& a, int num_sms, cudaStream_t st);
+
+// ---- sensory backward ----------------------------------------------------
+struct SensBwdArgs {
+  const float4* spack;  // [D][HP]
+  const float* x;       // (rows, D)
+  const float* gsn;     // (rows, H)
+  const float* gsd;     // (rows, H)
+  float* dx;            // (rows, D)   (nqc == 1) or dx partials [nqc][rows][D]
+  float* part;          // [nsplit][4][D][HP] synapse partials (A_n, A_d, DZ, DZX)
+  long long rows;
+  int D, H, HP;
+  int nsplit;           // row splits (gridDim.y)
+};
+struct SensBwdPlan {
+  int qc;          // columns per CTA
+  int nqc;         // column chunks
+  int dpc;         // inputs d per CTA
+  int ndc;         // d chunks
+  int nsplit;      // row splits
+  size_t part_floats;
+  size_t dxpart_floats;  // 0 when nqc == 1
+};
+SensBwdPlan plan_sensory_bwd(long long rows, int D, int HP, int num_sms);
+cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart,
+                               cudaStream_t st);
+
+// ---- recurrent forward / backward ----------------------------------------
+struct RecFwdArgs {
+  const float4* pack;   // [HP][HP]
+  const float4* nrn;    // [HP]
+  const float* sn;      // (B*T, H)
+  const float* sd;      // (B*T, H)
+  const float* h0;      // (B,H) or null (zeros)
+  float* out;           // (B,T,H)
+  float* hT;            // (B,H)
+  float* V;             // (T*U+1, B, H) or null
+  float* R;             // (T*U, B, H) or null
+  int B, T, H, U, HP;
+  int ns;               // samples per CTA
+  float eps;
+};
+struct RecBwdArgs {
+  const float4* pack;   // [HP][HP] (fast path)
+  const float4* packT;  // [HP][HP] (wide path)
+  const float4* nrn;
+  const float* V;
+  const float* R;
+  const float* gout;    // strided (B,T,H)
+  long long go_sb, go_st, go_sh;
+  const float* gstate;  // (B,H) or null
+  float* gsn;           // (B*T, H)
+  float* gsd;           // (B*T, H)
+  float* gh0;           // (B,H)
+  float* part;          // [slots][4][HP*HP]  synapse partials, layout [p][q] (fast) / [q][p] (wide)
+  float* partn;         // [slots][3][HP]
+  int B, T, H, U, HP;
+  int ns;
+};
+struct RecPlan {
+  bool wide;       // generic (wide-H) kernels instead of the register-resident ones
+  int HP;          // padded neuron count
+  int ns_fwd, grid_fwd, threads_fwd;
+  size_t smem_fwd;
+  int ns_bwd, grid_bwd, threads_bwd, slots_bwd;
+  size_t smem_bwd;
+};
+RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide);
+cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
+cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
+
+// ---- deterministic reductions and final gradient transforms --------------
+struct FinishArgs {
+  const float* rec_part;   // [rslots][4][HP*HP]
+  const float* rec_partn;  // [rslots][3][HP]
+  int rslots;
+  bool rec_transposed;     // partial layout [q][p]
+  const float* sens_part;  // [nsplit][4][D*HP]
+  int nsplit;
+  const float* dxpart;     // [nqc][rows*D] or null
+  int nqc;
+  long long rows;
+  // inputs needed by the transforms
+  const float* mu; const float* sigma;
+  const float* smu; const float* ssig; const float* serev; const float* sw;
+  // outputs
+  float* g_w_pos; float* g_w_erev; float* g_mu; float* g_sigma;
+  float* g_smu; float* g_ssig; float* g_serev; float* g_sw;
+  float* g_cm; float* g_gl; float* g_vl;
+  float* g_x;
+  int D, H, HP;
+};
+cudaError_t launch_finish(const FinishArgs& a, int num_sms, cudaStream_t st);
+
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+inline int pad_neurons(int H) { return H <= 32 ? 32 : (H <= 64 ? 64 : round_up(H, 32)); }
+
+}  // namespace ltc

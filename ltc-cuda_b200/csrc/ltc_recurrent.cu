@@ -1,0 +1,396 @@
+// Persistent recurrent kernels for H <= 64 (padded to HP = 32 or 64).
+//
+// One CTA owns a group of `ns` samples for the whole sequence (all T*U
+// unfolds in one launch) and keeps every recurrent synapse of the cell in
+// registers: HP*HP/8 threads, 8 synapses per thread, 4 gate-pack values per
+// synapse (and, in the backward kernel, 4 gradient accumulators per synapse).
+// Per unfold the only traffic is the sample state in shared memory; one
+// __syncthreads() separates unfolds (Jacobi update: every new v is computed
+// from the previous unfold's v, double-buffered -- unlike an in-place update).
+//
+// Forward thread map:  column q = tid / TPC, lane group g = tid % TPC (TPC = HP/8)
+//                      owns presynaptic rows p(j) = (j/4)*(HP/2) + 4g + j%4.
+// Backward thread map: row p = tid / TPC, owns columns q(j) with the same formula.
+// The interleaved p(j)/q(j) make the float4 shared-memory loads bank-conflict free.
+#include "ltc_common.cuh"
+#include "ltc_internal.h"
+
+namespace ltc {
+
+namespace {
+
+constexpr int kSB = 4;  // samples per register block
+
+template <int HP>
+struct Geometry {
+  static constexpr int TPC = HP / 8;
+  static constexpr int NT = HP * TPC;
+  static constexpr int LDV = HP + 4;  // padded row stride of per-sample vectors
+  __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (HP / 2) + 4 * g + (j % 4); }
+};
+
+template <int HP>
+__global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a) {
+  using G = Geometry<HP>;
+  constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV;
+  using LR = LaneReduce<TPC, kSB>;
+  extern __shared__ __align__(16) float smem[];
+  const int ns = a.ns;
+  float* vbuf = smem;                // [2][ns][LDV]
+  float* snb = vbuf + 2 * ns * LDV;  // [ns][LDV]
+  float* sdb = snb + ns * LDV;       // [ns][LDV]
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int q = tid / TPC, g = tid % TPC;
+  const int H = a.H, B = a.B, T = a.T, U = a.U;
+  const int b0 = blockIdx.x * ns;
+  const int nvalid = min(ns, B - b0);
+  const int nblk = (nvalid + kSB - 1) / kSB;
+
+  float sl[8], nm[8], wp[8], we[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 pk = a.pack[G::sub(j, g) * HP + q];
+    sl[j] = pk.x; nm[j] = pk.y; wp[j] = pk.z; we[j] = pk.w;
+  }
+  const float4 nq = a.nrn[q];
+  const float cm = nq.x, cmgl = nq.x + nq.y, glvl = nq.w;
+  const bool qvalid = q < H;
+  const int own = LR::own_base(lane);
+  const bool writer = LR::writer(lane);
+
+  for (int i = tid; i < 4 * ns * LDV; i += NT) smem[i] = 0.f;
+  __syncthreads();
+  if (a.h0) {
+    for (int i = tid; i < nvalid * H; i += NT) {
+      const int s = i / H, h = i % H;
+      vbuf[s * LDV + h] = a.h0[(long long)(b0 + s) * H + h];
+    }
+  }
+  int cur = 0;
+  for (int t = 0; t < T; ++t) {
+    __syncthreads();
+    for (int i = tid; i < nvalid * H; i += NT) {
+      const int s = i / H, h = i % H;
+      const long long row = (long long)(b0 + s) * T + t;
+      snb[s * LDV + h] = a.sn[row * H + h];
+      sdb[s * LDV + h] = a.sd[row * H + h];
+    }
+    __syncthreads();
+    for (int u = 0; u < U; ++u) {
+      const long long n = (long long)t * U + u;
+      const float* vc = vbuf + cur * ns * LDV;
+      float* vn = vbuf + (cur ^ 1) * ns * LDV;
+      for (int blk = 0; blk < nblk; ++blk) {
+        float acc[2][kSB];
+#pragma unroll
+        for (int i = 0; i < kSB; ++i) {
+          const float* vr = vc + (blk * kSB + i) * LDV + 4 * g;
+          const float4 va = *reinterpret_cast<const float4*>(vr);
+          const float4 vb = *reinterpret_cast<const float4*>(vr + HP / 2);
+          const float v8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+          float sn_ = 0.f, sd_ = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float act = gate(sl[j], nm[j], v8[j]);
+            sn_ = fmaf(we[j], act, sn_);
+            sd_ = fmaf(wp[j], act, sd_);
+          }
+          acc[0][i] = sn_;
+          acc[1][i] = sd_;
+        }
+        LR::template run<2>(acc, lane);
+#pragma unroll
+        for (int o = 0; o < LR::OWN; ++o) {
+          const int s = blk * kSB + own + o;
+          const float v = vc[s * LDV + q];
+          const float wn = acc[0][o] + snb[s * LDV + q];
+          const float wd = acc[1][o] + sdb[s * LDV + q];
+          const float num = (cm * v + glvl) + wn;
+          const float r = rcp_approx((cmgl + wd) + a.eps);
+          const float vnew = num * r;
+          if (qvalid && writer && s < nvalid) {
+            vn[s * LDV + q] = vnew;
+            const long long bs = b0 + s;
+            if (a.V) {
+              a.V[(n * B + bs) * H + q] = v;
+              a.R[(n * B + bs) * H + q] = r;
+            }
+            if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
+          }
+        }
+      }
+      __syncthreads();
+      cur ^= 1;
+    }
+  }
+  const float* vc = vbuf + cur * ns * LDV;
+  for (int i = tid; i < nvalid * H; i += NT) {
+    const int s = i / H, h = i % H;
+    const long long bs = b0 + s;
+    a.hT[bs * H + h] = vc[s * LDV + h];
+    if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[s * LDV + h];
+  }
+}
+
+// Backward: reverse sweep over n = T*U-1 .. 0 with the adjoint of each unfold.
+//  AN/AD[s][q]   = a_n = g*r, a_d = -g*v'*r of the unfold being processed
+//  VS[n%3][s][.] = saved V[n] (3 buffers: current, next, prefetch)
+//  RS[n%2][s][.] = saved R[n]
+//  DIR[s][p]     = direct term g*cm*r of the unfold being processed
+//  GSN/GSD[s][p] = running sums of a_n / a_d over the unfolds of the current step
+template <int HP>
+__global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a) {
+  using G = Geometry<HP>;
+  constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV;
+  using LR = LaneReduce<TPC, kSB>;
+  extern __shared__ __align__(16) float smem[];
+  const int ns = a.ns;
+  const int SL = ns * LDV;  // one per-sample slab
+  float* AN = smem;          // [2]
+  float* AD = AN + 2 * SL;   // [2]
+  float* VS = AD + 2 * SL;   // [3]
+  float* RS = VS + 3 * SL;   // [2]
+  float* DIR = RS + 2 * SL;
+  float* GSN = DIR + SL;
+  float* GSD = GSN + SL;     // total 13 slabs
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int p = tid / TPC, g = tid % TPC;
+  const int H = a.H, B = a.B, T = a.T, U = a.U;
+  const int b0 = blockIdx.x * ns;
+  const int nvalid = min(ns, B - b0);
+  const int nblk = (nvalid + kSB - 1) / kSB;
+  const long long NTU = (long long)T * U;
+
+  float sl[8], nm[8], wp[8], we[8];
+  float Gwe[8], Gwp[8], Gdz[8], Gdzv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 pk = a.pack[p * HP + G::sub(j, g)];
+    sl[j] = pk.x; nm[j] = pk.y; wp[j] = pk.z; we[j] = pk.w;
+    Gwe[j] = Gwp[j] = Gdz[j] = Gdzv[j] = 0.f;
+  }
+  const float4 np_ = a.nrn[p];
+  const float cm = np_.x, gl = np_.y, vl = np_.z;
+  const bool pvalid = p < H;
+  const int own = LR::own_base(lane);
+  const bool writer = LR::writer(lane);
+  float gcm = 0.f, ggl = 0.f, gvl = 0.f;
+
+  for (int i = tid; i < 13 * SL; i += NT) smem[i] = 0.f;
+  __syncthreads();
+
+  // stage saved slices: V[m] -> VS[m%3], R[m] -> RS[m%2]
+  auto stage_v = [&](long long m) {
+    float* dst = VS + (int)(m % 3) * SL;
+    const float* src = a.V + m * B * H + (long long)b0 * H;
+    for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
+  };
+  auto stage_r = [&](long long m) {
+    float* dst = RS + (int)(m % 2) * SL;
+    const float* src = a.R + m * B * H + (long long)b0 * H;
+    for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
+  };
+  stage_v(NTU);
+  stage_v(NTU - 1);
+  stage_r(NTU - 1);
+  if (NTU >= 2) {
+    stage_v(NTU - 2);
+    stage_r(NTU - 2);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+
+  // Per-neuron prep of unfold m for (sample s, neuron p) given g = dL/dv_{m+1}[p].
+  auto prep = [&](long long m, int s, float gval, bool first_of_step) {
+    const float r = RS[(int)(m % 2) * SL + s * LDV + p];
+    const float vin = VS[(int)(m % 3) * SL + s * LDV + p];
+    const float vout = VS[(int)((m + 1) % 3) * SL + s * LDV + p];
+    const float an = gval * r;
+    const float ad = -an * vout;
+    gcm = fmaf(an, vin - vout, gcm);
+    ggl = fmaf(an, vl - vout, ggl);
+    gvl = fmaf(an, gl, gvl);
+    const int idx = s * LDV + p;
+    GSN[idx] = first_of_step ? an : GSN[idx] + an;
+    GSD[idx] = first_of_step ? ad : GSD[idx] + ad;
+    DIR[idx] = an * cm;
+    AN[(int)(m % 2) * SL + idx] = an;
+    AD[(int)(m % 2) * SL + idx] = ad;
+  };
+
+  // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate
+  if (pvalid) {
+    for (int blk = 0; blk < nblk; ++blk) {
+#pragma unroll
+      for (int o = 0; o < LR::OWN; ++o) {
+        const int s = blk * kSB + own + o;
+        if (writer && s < nvalid) {
+          const long long bs = b0 + s;
+          float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
+          if (a.gstate) gval += a.gstate[bs * H + p];
+          prep(NTU - 1, s, gval, true);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  for (long long n = NTU - 1; n >= 0; --n) {
+    // Tails of iteration m read V[m-1], V[m] and R[m-1]; prefetch what the tails
+    // of the next iteration (n-1) need beyond that: V[n-2] and R[n-2].  Their
+    // slots ((n+1)%3 and n%2) are not read in this iteration.
+    if (n >= 2) {
+      stage_v(n - 2);
+      stage_r(n - 2);
+    }
+    cp_async_commit();
+
+    const int ci = (int)(n % 2);
+    const float* an_s = AN + ci * SL;
+    const float* ad_s = AD + ci * SL;
+    const float* vsn = VS + (int)(n % 3) * SL;
+    const int t = (int)(n / U), k = (int)(n % U);
+    for (int blk = 0; blk < nblk; ++blk) {
+      float acc[1][kSB];
+#pragma unroll
+      for (int i = 0; i < kSB; ++i) {
+        const int s = blk * kSB + i;
+        const float vp = vsn[s * LDV + p];
+        const float* ar = an_s + s * LDV + 4 * g;
+        const float* dr = ad_s + s * LDV + 4 * g;
+        const float4 a0 = *reinterpret_cast<const float4*>(ar);
+        const float4 a1 = *reinterpret_cast<const float4*>(ar + HP / 2);
+        const float4 d0 = *reinterpret_cast<const float4*>(dr);
+        const float4 d1 = *reinterpret_cast<const float4*>(dr + HP / 2);
+        const float an8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float ad8[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        float dv = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float act = gate(sl[j], nm[j], vp);
+          const float sp = fmaf(-act, act, act);
+          const float dz = fmaf(an8[j], we[j], ad8[j] * wp[j]) * sp;
+          Gwe[j] = fmaf(an8[j], act, Gwe[j]);
+          Gwp[j] = fmaf(ad8[j], act, Gwp[j]);
+          Gdz[j] += dz;
+          Gdzv[j] = fmaf(dz, vp, Gdzv[j]);
+          dv = fmaf(dz, sl[j], dv);
+        }
+        acc[0][i] = dv;
+      }
+      LR::template run<1>(acc, lane);
+      if (pvalid && writer) {
+#pragma unroll
+        for (int o = 0; o < LR::OWN; ++o) {
+          const int s = blk * kSB + own + o;
+          if (s < nvalid) {
+            const int idx = s * LDV + p;
+            float gval = DIR[idx] - acc[0][o] * LTC_LN2;  // dL/dv_n[p]
+            const long long bs = b0 + s;
+            if (k == 0) {
+              const long long row = bs * T + t;
+              a.gsn[row * H + p] = GSN[idx];
+              a.gsd[row * H + p] = GSD[idx];
+              if (t == 0) {
+                a.gh0[bs * H + p] = gval;
+                continue;
+              }
+              gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
+            }
+            prep(n - 1, s, gval, k == 0);
+          }
+        }
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+  }
+
+  // partial gradients of this CTA
+  float* part = a.part + (long long)blockIdx.x * 4 * HP * HP;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int idx = p * HP + G::sub(j, g);
+    part[idx] = Gwe[j];
+    part[HP * HP + idx] = Gwp[j];
+    part[2 * HP * HP + idx] = Gdz[j];
+    part[3 * HP * HP + idx] = Gdzv[j];
+  }
+#pragma unroll
+  for (int stride = TPC / 2; stride >= 1; stride >>= 1) {
+    gcm += __shfl_xor_sync(0xffffffffu, gcm, stride);
+    ggl += __shfl_xor_sync(0xffffffffu, ggl, stride);
+    gvl += __shfl_xor_sync(0xffffffffu, gvl, stride);
+  }
+  if (g == 0) {
+    float* pn = a.partn + (long long)blockIdx.x * 3 * HP;
+    pn[p] = gcm;
+    pn[HP + p] = ggl;
+    pn[2 * HP + p] = gvl;
+  }
+}
+
+template <int HP>
+cudaError_t launch_fast_fwd(const RecFwdArgs& a, const RecPlan& pl, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(rec_fwd_fast<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)pl.smem_fwd);
+  if (e != cudaSuccess) return e;
+  rec_fwd_fast<HP><<<pl.grid_fwd, Geometry<HP>::NT, pl.smem_fwd, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int HP>
+cudaError_t launch_fast_bwd(const RecBwdArgs& a, const RecPlan& pl, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(rec_bwd_fast<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)pl.smem_bwd);
+  if (e != cudaSuccess) return e;
+  rec_bwd_fast<HP><<<pl.grid_bwd, Geometry<HP>::NT, pl.smem_bwd, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// wide-H kernels (ltc_recurrent_wide.cu)
+cudaError_t launch_wide_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
+cudaError_t launch_wide_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
+void plan_wide(RecPlan& p, int B, int H, int num_sms);
+
+RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
+  RecPlan p{};
+  p.HP = pad_neurons(H);
+  p.wide = force_wide || H > 64;
+  if (p.wide) {
+    plan_wide(p, B, H, num_sms);
+    return p;
+  }
+  const int HP = p.HP;
+  const int LDV = HP + 4;
+  const int blocks = (B + kSB - 1) / kSB;
+  // one CTA per SM when possible, each owning an equal share of sample blocks
+  int per = (blocks + num_sms - 1) / num_sms;
+  const int max_per = 64 / kSB;  // shared-memory bound for the backward kernel
+  if (per > max_per) per = max_per;
+  if (per < 1) per = 1;
+  p.ns_fwd = p.ns_bwd = per * kSB;
+  p.grid_fwd = p.grid_bwd = (B + p.ns_fwd - 1) / p.ns_fwd;
+  p.threads_fwd = p.threads_bwd = HP * HP / 8;
+  p.slots_bwd = p.grid_bwd;
+  p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
+  p.smem_bwd = (size_t)13 * p.ns_bwd * LDV * sizeof(float);
+  return p;
+}
+
+cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  if (p.wide) return launch_wide_fwd(a, p, st);
+  return p.HP == 32 ? launch_fast_fwd<32>(a, p, st) : launch_fast_fwd<64>(a, p, st);
+}
+
+cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  if (p.wide) return launch_wide_bwd(a, p, st);
+  return p.HP == 32 ? launch_fast_bwd<32>(a, p, st) : launch_fast_bwd<64>(a, p, st);
+}
+
+}  // namespace ltc

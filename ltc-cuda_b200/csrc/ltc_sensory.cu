@@ -1,0 +1,273 @@
+// Sensory conductance pass, forward and backward, batched over all B*T rows.
+//
+// The sensory term  sn[q] = sum_d sw*serev*act,  sd[q] = sum_d sw*act,
+// act = sigmoid(ssig*(x[d]-smu)), does not depend on the state, so it is
+// computed for every (b,t) row in one launch before the recurrence
+// (row = b*T + t, x is (rows, D)).
+//
+// Forward: thread = (column q, row group rg), RB rows per thread, no
+//   cross-thread reduction; the gate pack of a chunk of DC inputs and the x
+//   tile are staged in shared memory and shared by the row groups.
+// Backward: thread = (input d, lane group g) owning 8 columns of a QC-column
+//   chunk (the same map as the recurrent backward kernel with p -> d); it
+//   accumulates the 4 synapse-gradient sums in registers over all rows of its
+//   row split and writes them once; dx[row][d] is reduced over the TPC lanes.
+#include "ltc_common.cuh"
+#include "ltc_internal.h"
+
+namespace ltc {
+
+namespace {
+
+constexpr int kRB = 8;  // rows per thread (forward)
+constexpr int kSB = 4;  // rows per register block (backward)
+constexpr int kRT = 32; // rows per staged tile (backward)
+
+struct SensFwdGeom {
+  int HPW, RG, NT, TR, DC;
+};
+
+__host__ __device__ inline SensFwdGeom sens_fwd_geom(int HPW, int D) {
+  SensFwdGeom g;
+  g.HPW = HPW;
+  g.RG = 512 / HPW;
+  g.NT = HPW * g.RG;
+  g.TR = g.RG * kRB;
+  int dc = 4096 / HPW;
+  if (dc < 4) dc = 4;
+  if (dc > D) dc = D;
+  g.DC = dc;
+  return g;
+}
+
+__global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  const SensFwdGeom G = sens_fwd_geom(a.HP, a.D);
+  float4* pks = reinterpret_cast<float4*>(smem);  // [DC][HPW]
+  float* xs = smem + 4 * G.DC * G.HPW;           // [DC][TR]
+  const int tid = threadIdx.x;
+  const int q = tid % G.HPW, rg = tid / G.HPW;
+  const int H = a.H, D = a.D;
+  const long long ntiles = (a.rows + G.TR - 1) / G.TR;
+  for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const long long row0 = tile * G.TR;
+    float sn[kRB], sd[kRB];
+#pragma unroll
+    for (int r = 0; r < kRB; ++r) sn[r] = sd[r] = 0.f;
+    for (int d0 = 0; d0 < D; d0 += G.DC) {
+      const int dc = min(G.DC, D - d0);
+      __syncthreads();
+      for (int i = tid; i < dc * G.HPW; i += blockDim.x) pks[i] = a.spack[(long long)d0 * G.HPW + i];
+      for (int i = tid; i < G.TR * dc; i += blockDim.x) {
+        const int r = i / dc, dd = i % dc;
+        const long long row = row0 + r;
+        xs[dd * G.TR + r] = row < a.rows ? a.x[row * D + d0 + dd] : 0.f;
+      }
+      __syncthreads();
+      const float* xr = xs + rg * kRB;
+      for (int dd = 0; dd < dc; ++dd) {
+        const float4 w = pks[dd * G.HPW + q];
+        const float4 x0 = *reinterpret_cast<const float4*>(xr + dd * G.TR);
+        const float4 x1 = *reinterpret_cast<const float4*>(xr + dd * G.TR + 4);
+        const float xv[kRB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int r = 0; r < kRB; ++r) {
+          const float act = gate(w.x, w.y, xv[r]);
+          sn[r] = fmaf(w.w, act, sn[r]);
+          sd[r] = fmaf(w.z, act, sd[r]);
+        }
+      }
+    }
+    if (q < H) {
+#pragma unroll
+      for (int r = 0; r < kRB; ++r) {
+        const long long row = row0 + rg * kRB + r;
+        if (row < a.rows) {
+          a.sn[row * H + q] = sn[r];
+          a.sd[row * H + q] = sd[r];
+        }
+      }
+    }
+  }
+}
+
+template <int QC>
+struct SensBwdGeom {
+  static constexpr int TPC = QC / 8;
+  static constexpr int DPC = 4096 / QC;  // inputs per CTA (512 threads)
+  static constexpr int LDG = QC + 4;
+  __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (QC / 2) + 4 * g + (j % 4); }
+};
+
+template <int QC>
+__global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc, long long rows_per_split,
+                                                          float* dxpart) {
+  using G = SensBwdGeom<QC>;
+  constexpr int TPC = G::TPC, DPC = G::DPC, LDG = G::LDG;
+  using LR = LaneReduce<TPC, kSB>;
+  extern __shared__ __align__(16) float smem[];
+  float* GN = smem;               // [kRT][LDG]
+  float* GD = GN + kRT * LDG;     // [kRT][LDG]
+  float* XS = GD + kRT * LDG;     // [kRT][DPC]
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int dl = tid / TPC, g = tid % TPC;
+  const int dchunk = blockIdx.x / nqc, qc = blockIdx.x % nqc;
+  const int d0 = dchunk * DPC, q0 = qc * QC;
+  const int d = d0 + dl;
+  const int D = a.D, H = a.H, HP = a.HP;
+  const bool dvalid = d < D;
+
+  float sl[8], nm[8], sw[8], swe[8];
+  float An[8], Ad[8], Dz[8], Dzx[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (dvalid) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
+    sl[j] = pk.x; nm[j] = pk.y; sw[j] = pk.z; swe[j] = pk.w;
+    An[j] = Ad[j] = Dz[j] = Dzx[j] = 0.f;
+  }
+  const int own = LR::own_base(lane);
+  const bool writer = LR::writer(lane);
+  const int hq = min(QC, H - q0);  // valid columns of this chunk
+  const long long r_begin = blockIdx.y * rows_per_split;
+  const long long r_end = min(a.rows, r_begin + rows_per_split);
+  const long long ndx = a.rows * D;
+
+  for (long long rt = r_begin; rt < r_end; rt += kRT) {
+    const int nr = (int)min((long long)kRT, r_end - rt);
+    __syncthreads();
+    for (int i = tid; i < kRT * QC; i += 512) {
+      const int r = i / QC, c = i % QC;
+      const bool ok = r < nr && c < hq;
+      const long long src = (rt + r) * H + q0 + c;
+      GN[r * LDG + c] = ok ? a.gsn[src] : 0.f;
+      GD[r * LDG + c] = ok ? a.gsd[src] : 0.f;
+    }
+    for (int i = tid; i < kRT * DPC; i += 512) {
+      const int r = i / DPC, c = i % DPC;
+      XS[i] = (r < nr && d0 + c < D) ? a.x[(rt + r) * D + d0 + c] : 0.f;
+    }
+    __syncthreads();
+    const int nblk = (nr + kSB - 1) / kSB;
+    for (int blk = 0; blk < nblk; ++blk) {
+      float acc[1][kSB];
+#pragma unroll
+      for (int i = 0; i < kSB; ++i) {
+        const int r = blk * kSB + i;
+        const float xv = XS[r * DPC + dl];
+        const float* ar = GN + r * LDG + 4 * g;
+        const float* dr = GD + r * LDG + 4 * g;
+        const float4 a0 = *reinterpret_cast<const float4*>(ar);
+        const float4 a1 = *reinterpret_cast<const float4*>(ar + QC / 2);
+        const float4 e0 = *reinterpret_cast<const float4*>(dr);
+        const float4 e1 = *reinterpret_cast<const float4*>(dr + QC / 2);
+        const float an8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float ad8[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+        float dxs = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float act = gate(sl[j], nm[j], xv);
+          const float sp = fmaf(-act, act, act);
+          const float dz = fmaf(an8[j], swe[j], ad8[j] * sw[j]) * sp;
+          An[j] = fmaf(an8[j], act, An[j]);
+          Ad[j] = fmaf(ad8[j], act, Ad[j]);
+          Dz[j] += dz;
+          Dzx[j] = fmaf(dz, xv, Dzx[j]);
+          dxs = fmaf(dz, sl[j], dxs);
+        }
+        acc[0][i] = dxs;
+      }
+      LR::template run<1>(acc, lane);
+      if (dvalid && writer) {
+#pragma unroll
+        for (int o = 0; o < LR::OWN; ++o) {
+          const int r = blk * kSB + own + o;
+          if (r < nr) {
+            const float v = -acc[0][o] * LTC_LN2;
+            const long long idx = (rt + r) * D + d;
+            if (nqc == 1) a.dx[idx] = v;
+            else dxpart[qc * ndx + idx] = v;
+          }
+        }
+      }
+    }
+  }
+  if (dvalid) {
+    const long long slab = (long long)D * HP;
+    float* part = a.part + (long long)blockIdx.y * 4 * slab + (long long)d * HP + q0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = G::sub(j, g);
+      part[c] = An[j];
+      part[slab + c] = Ad[j];
+      part[2 * slab + c] = Dz[j];
+      part[3 * slab + c] = Dzx[j];
+    }
+  }
+}
+
+int pick_qc(int HP) {
+  for (int qc = 256; qc >= 32; qc >>= 1)
+    if (HP % qc == 0) return qc;
+  return 32;
+}
+
+}  // namespace
+
+cudaError_t launch_sensory_fwd(const SensFwdArgs& a, int num_sms, cudaStream_t st) {
+  if (a.rows <= 0) return cudaSuccess;
+  const SensFwdGeom G = sens_fwd_geom(a.HP, a.D);
+  const size_t smem = (size_t)G.DC * G.HPW * 16 + (size_t)G.DC * G.TR * 4;
+  cudaError_t e = cudaFuncSetAttribute(sens_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const long long ntiles = (a.rows + G.TR - 1) / G.TR;
+  const int per_sm = (G.NT <= 512 && smem <= 110 * 1024) ? 2 : 1;
+  const long long grid = ntiles < (long long)num_sms * per_sm ? ntiles : (long long)num_sms * per_sm;
+  sens_fwd_kernel<<<(int)grid, G.NT, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+SensBwdPlan plan_sensory_bwd(long long rows, int D, int HP, int num_sms) {
+  SensBwdPlan p{};
+  p.qc = pick_qc(HP);
+  p.nqc = HP / p.qc;
+  p.dpc = 4096 / p.qc;
+  p.ndc = (D + p.dpc - 1) / p.dpc;
+  int ns = num_sms / (p.ndc * p.nqc);
+  if (ns < 1) ns = 1;
+  const long long max_split = (rows + kRT - 1) / kRT;
+  if (ns > max_split) ns = (int)(max_split > 0 ? max_split : 1);
+  p.nsplit = ns;
+  p.part_floats = (size_t)ns * 4 * D * HP;
+  p.dxpart_floats = p.nqc > 1 ? (size_t)p.nqc * rows * D : 0;
+  return p;
+}
+
+cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart, cudaStream_t st) {
+  if (a.rows <= 0) return cudaSuccess;
+  long long rps = (a.rows + p.nsplit - 1) / p.nsplit;
+  rps = (rps + kRT - 1) / kRT * kRT;
+  dim3 grid(p.ndc * p.nqc, p.nsplit);
+  const size_t smem = (size_t)2 * kRT * (p.qc + 4) * 4 + (size_t)kRT * p.dpc * 4;
+  cudaError_t e;
+#define LTC_SB_CASE(QCV)                                                                          \
+  case QCV:                                                                                       \
+    e = cudaFuncSetAttribute(sens_bwd_kernel<QCV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             (int)smem);                                                         \
+    if (e != cudaSuccess) return e;                                                               \
+    sens_bwd_kernel<QCV><<<grid, 512, smem, st>>>(a, p.nqc, rps, dxpart);                         \
+    break;
+  switch (p.qc) {
+    LTC_SB_CASE(32)
+    LTC_SB_CASE(64)
+    LTC_SB_CASE(128)
+    LTC_SB_CASE(256)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef LTC_SB_CASE
+  return cudaGetLastError();
+}
+
+}  // namespace ltc

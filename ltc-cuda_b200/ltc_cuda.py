@@ -1,0 +1,326 @@
+"""Drop-in ``ltc_cuda`` for the LTC ODE solver, backed by libltc_sm100.so (sm_100a).
+
+This module keeps the names and call signatures the reference's ``ltc.py``
+imports (``from ltc_cuda import _HAS_CUDA_KERNELS, ltc_cuda_forward``,
+``ltc.py:12-16``) and the reference's bridge exposes (``ltc_cuda.py:241-388``):
+
+* ``_HAS_CUDA_KERNELS``  -- True when the library loaded and a CUDA device is present
+* ``ltc_cuda_forward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu,
+  sensory_sigma, sensory_erev, sensory_w_pos, cm_t, gleak_pos, vleak,
+  ode_unfolds, epsilon) -> (outputs, state)``  (``ltc_cuda.py:362-388``)
+* ``LTCCudaForward``     -- the autograd.Function (``ltc_cuda.py:241-359``): forward
+  takes the same 15 inputs plus ``needs_grad``; backward returns 13 gradients
+  in input order followed by three ``None``
+* ``_cuda_module.ltc_full_forward`` / ``ltc_full_backward`` -- the whole-sequence
+  forward/backward calls (``csrc/ltc_kernels.cu:1165``, ``:962``)
+
+Differences from the reference bridge, all internal to this module: parameters
+are passed untransposed (no transposed copies are made), the forward saves one
+opaque buffer (per-unfold states and reciprocal denominators) instead of the
+(T,U,B,H) state stack plus the two sensory stacks, and every kernel runs on
+PyTorch's current stream instead of the legacy default stream.
+
+There is no fallback inside this module: on a machine with CUDA, a missing or
+unloadable library raises at import; calling ``ltc_cuda_forward`` without CUDA
+kernels raises ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import logging
+import os
+from typing import List, Optional, Sequence
+
+import torch
+
+logger = logging.getLogger(__name__)
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("LTC_SM100_LIB", os.path.join(_HERE, "libltc_sm100.so"))
+
+LTC_FLAG_FORCE_WIDE = 1
+
+
+class LtcDims(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("T", ctypes.c_int32), ("D", ctypes.c_int32), ("H", ctypes.c_int32),
+                ("ode_unfolds", ctypes.c_int32), ("epsilon", ctypes.c_float), ("flags", ctypes.c_int32)]
+
+
+class LtcParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "w_pos", "w_erev", "mu", "sigma", "sensory_mu", "sensory_sigma", "sensory_erev",
+        "sensory_w_pos", "cm_t", "gleak_pos", "vleak")]
+
+
+class LtcGrads(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "x_seq", "state", "w_pos", "w_erev", "mu", "sigma", "sensory_mu", "sensory_sigma",
+        "sensory_erev", "sensory_w_pos", "cm_t", "gleak_pos", "vleak")]
+
+
+class LtcPlan(ctypes.Structure):
+    _fields_ = [("saved_bytes", ctypes.c_size_t), ("fwd_workspace_bytes", ctypes.c_size_t),
+                ("bwd_workspace_bytes", ctypes.c_size_t), ("wide", ctypes.c_int32),
+                ("padded_h", ctypes.c_int32), ("fwd_ctas", ctypes.c_int32), ("bwd_ctas", ctypes.c_int32)]
+
+
+# Exported symbols and their C signatures (include/ltc_sm100.h).
+EXPORTS = {
+    "ltc_plan": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcPlan)]),
+    "ltc_forward": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams), ctypes.c_void_p,
+                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                   ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_backward": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams), ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64),
+                                    ctypes.c_void_p, ctypes.POINTER(LtcGrads), ctypes.c_void_p,
+                                    ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
+    "ltc_timing_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32),
+                                          ctypes.c_int]),
+    "ltc_launch_count": (ctypes.c_int64, []),
+    "ltc_last_error": (ctypes.c_char_p, []),
+    "ltc_version": (ctypes.c_int, []),
+}
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_lib: Optional[ctypes.CDLL] = None
+_load_error: Optional[str] = None
+try:
+    _lib = load_library()
+except OSError as exc:  # library not built
+    _load_error = str(exc)
+
+if _lib is None and torch.cuda.is_available():
+    raise RuntimeError(
+        f"ltc_cuda: CUDA is available but {LIB_PATH} could not be loaded ({_load_error}); "
+        "build it with `python ltc-cuda_b200/build.py` (there is no CPU/TorchScript fallback)")
+
+_HAS_CUDA_KERNELS: bool = _lib is not None and torch.cuda.is_available()
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        msg = _lib.ltc_last_error().decode(errors="replace") if _lib is not None else "library not loaded"
+        raise RuntimeError(f"ltc_cuda.{what} failed: {msg}")
+
+
+def _require_kernels() -> ctypes.CDLL:
+    if not _HAS_CUDA_KERNELS:
+        raise RuntimeError("ltc_cuda: CUDA kernels unavailable "
+                           f"(library: {_load_error or 'loaded'}, cuda: {torch.cuda.is_available()})")
+    return _lib
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _as_f32(t: torch.Tensor, device: torch.device, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32 (got {t.dtype})")
+    return t.contiguous()
+
+
+def make_dims(B: int, T: int, D: int, H: int, ode_unfolds: int, epsilon: float, flags: int = 0) -> LtcDims:
+    return LtcDims(int(B), int(T), int(D), int(H), int(ode_unfolds), float(epsilon), int(flags))
+
+
+def plan(dims: LtcDims) -> LtcPlan:
+    lib = _require_kernels()
+    p = LtcPlan()
+    _check(lib.ltc_plan(ctypes.byref(dims), ctypes.byref(p)), "ltc_plan")
+    return p
+
+
+_flags = 0
+
+
+def set_force_wide(on: bool) -> None:
+    """Route every call through the streamed wide-H kernels (testing the second path)."""
+    global _flags
+    _flags = LTC_FLAG_FORCE_WIDE if on else 0
+
+
+KERNEL_NAMES = ("pack_fwd", "sensory_fwd", "recurrent_fwd", "pack_bwd", "recurrent_bwd", "sensory_bwd",
+                "finish")
+
+
+def timing_enable(on: bool) -> None:
+    """Bracket every library launch with CUDA events on its own stream (see ltc_timing_enable)."""
+    _check(_require_kernels().ltc_timing_enable(1 if on else 0), "ltc_timing_enable")
+
+
+def timing_collect() -> dict:
+    """{kernel name: (total ms, launches)} since timing was enabled or last collected."""
+    lib = _require_kernels()
+    n = len(KERNEL_NAMES)
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_int32 * n)()
+    _check(lib.ltc_timing_collect(ms, cnt, n), "ltc_timing_collect")
+    return {k: (ms[i], cnt[i]) for i, k in enumerate(KERNEL_NAMES)}
+
+
+def launch_count() -> int:
+    return int(_require_kernels().ltc_launch_count())
+
+
+def _params_struct(ts: Sequence[torch.Tensor]) -> LtcParams:
+    return LtcParams(*[t.data_ptr() for t in ts])
+
+
+class _CudaModule:
+    """Whole-sequence calls with the reference's names (``csrc/ltc_kernels.cu:1307-1314``)."""
+
+    @staticmethod
+    def ltc_full_forward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma, sensory_erev,
+                         sensory_w_pos, cm_t, gleak_pos, vleak, ode_unfolds: int, epsilon: float,
+                         save_intermediates: bool) -> List[torch.Tensor]:
+        """Returns [outputs (B,T,H), final state (B,H)] (+ [saved] when save_intermediates)."""
+        lib = _require_kernels()
+        dev = x_seq.device
+        x = _as_f32(x_seq, dev, "x_seq")
+        B, T, D = x.shape
+        H = state.shape[1]
+        h0 = _as_f32(state, dev, "state")
+        params = [_as_f32(t, dev, n) for t, n in zip(
+            (w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma, sensory_erev, sensory_w_pos,
+             cm_t, gleak_pos, vleak),
+            ("w_pos", "w_erev", "mu", "sigma", "sensory_mu", "sensory_sigma", "sensory_erev",
+             "sensory_w_pos", "cm_t", "gleak_pos", "vleak"))]
+        _check_shapes(B, T, D, H, params)
+        outputs = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        if B == 0 or T == 0 or int(ode_unfolds) <= 0:
+            return _degenerate_forward(x, h0, outputs, save_intermediates)
+        dims = make_dims(B, T, D, H, ode_unfolds, epsilon, _flags)
+        with torch.cuda.device(dev):
+            pl = plan(dims)
+            h_final = torch.empty(B, H, device=dev, dtype=torch.float32)
+            saved = torch.empty(pl.saved_bytes, device=dev, dtype=torch.uint8) if save_intermediates else None
+            ws = torch.empty(pl.fwd_workspace_bytes, device=dev, dtype=torch.uint8)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _check(lib.ltc_forward(ctypes.byref(dims), ctypes.byref(_params_struct(params)), x.data_ptr(),
+                                   h0.data_ptr(), outputs.data_ptr(), h_final.data_ptr(), _ptr(saved),
+                                   ws.data_ptr(), pl.fwd_workspace_bytes, stream), "ltc_full_forward")
+        return [outputs, h_final, saved] if save_intermediates else [outputs, h_final]
+
+    @staticmethod
+    def ltc_full_backward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma, sensory_erev,
+                          sensory_w_pos, cm_t, gleak_pos, vleak, saved, grad_outputs, grad_final_state,
+                          ode_unfolds: int, epsilon: float, has_grad_state: bool) -> List[torch.Tensor]:
+        """13 gradients in the order of the forward inputs (``ltc_cuda.py:342-355``)."""
+        lib = _require_kernels()
+        dev = x_seq.device
+        x = _as_f32(x_seq, dev, "x_seq")
+        B, T, D = x.shape
+        H = state.shape[1]
+        params = [_as_f32(t, dev, "param") for t in (w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma,
+                                                     sensory_erev, sensory_w_pos, cm_t, gleak_pos, vleak)]
+        if grad_outputs is None:
+            grad_outputs = torch.zeros(1, device=dev, dtype=torch.float32).expand(B, T, H)
+        elif grad_outputs.dtype != torch.float32:
+            grad_outputs = grad_outputs.float()
+        gs = None
+        if has_grad_state and grad_final_state is not None:
+            gs = _as_f32(grad_final_state, dev, "grad_final_state")
+        grads = [torch.empty(B, T, D, device=dev), torch.empty(B, H, device=dev)] + \
+                [torch.empty_like(p) for p in params]
+        dims = make_dims(B, T, D, H, ode_unfolds, epsilon, _flags)
+        strides = (ctypes.c_int64 * 3)(*grad_outputs.stride())
+        with torch.cuda.device(dev):
+            pl = plan(dims)
+            ws = torch.empty(pl.bwd_workspace_bytes, device=dev, dtype=torch.uint8)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _check(lib.ltc_backward(ctypes.byref(dims), ctypes.byref(_params_struct(params)), x.data_ptr(),
+                                    saved.data_ptr(), grad_outputs.data_ptr(), strides, _ptr(gs),
+                                    ctypes.byref(LtcGrads(*[g.data_ptr() for g in grads])), ws.data_ptr(),
+                                    pl.bwd_workspace_bytes, stream), "ltc_full_backward")
+        return grads
+
+
+_cuda_module = _CudaModule()
+
+
+def _check_shapes(B, T, D, H, params):
+    expect = [(H, H)] * 4 + [(D, H)] * 4 + [(H,)] * 3
+    names = ("w_pos", "w_erev", "mu", "sigma", "sensory_mu", "sensory_sigma", "sensory_erev",
+             "sensory_w_pos", "cm_t", "gleak_pos", "vleak")
+    for t, e, n in zip(params, expect, names):
+        if tuple(t.shape) != e:
+            raise ValueError(f"{n} has shape {tuple(t.shape)}, expected {e}")
+
+
+def _degenerate_forward(x, h0, outputs, save_intermediates):
+    """B == 0, T == 0 or no unfolds: the state passes through unchanged (``ltc.py:50-63,96-104``)."""
+    B, T = x.shape[:2]
+    if T > 0 and B > 0:
+        outputs.copy_(h0.unsqueeze(1).expand(B, T, h0.shape[1]))
+    h = h0.clone()
+    return [outputs, h, torch.empty(0, dtype=torch.uint8, device=x.device)] if save_intermediates else [outputs, h]
+
+
+class LTCCudaForward(torch.autograd.Function):
+    """Autograd bridge with the reference's argument order (``ltc_cuda.py:241-359``)."""
+
+    @staticmethod
+    def forward(ctx, x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma, sensory_erev,
+                sensory_w_pos, cm_t, gleak_pos, vleak, ode_unfolds: int, epsilon: float, needs_grad: bool):
+        res = _cuda_module.ltc_full_forward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma,
+                                            sensory_erev, sensory_w_pos, cm_t, gleak_pos, vleak,
+                                            ode_unfolds, epsilon, needs_grad)
+        outputs, h = res[0], res[1]
+        if needs_grad:
+            ctx.save_for_backward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma,
+                                  sensory_erev, sensory_w_pos, cm_t, gleak_pos, vleak, res[2])
+        ctx.ode_unfolds = int(ode_unfolds)
+        ctx.epsilon = float(epsilon)
+        ctx.set_materialize_grads(False)
+        return outputs, h
+
+    @staticmethod
+    def backward(ctx, grad_outputs, grad_state):
+        saved = ctx.saved_tensors
+        if not saved:
+            raise RuntimeError("LTCCudaForward.backward: forward ran with needs_grad=False")
+        (x_seq, state, w_pos, w_erev, mu, sigma, smu, ssig, serev, sw, cm_t, gleak_pos, vleak, buf) = saved
+        B, T, _ = x_seq.shape
+        H = state.shape[1]
+        if B == 0 or T == 0 or ctx.ode_unfolds <= 0:
+            return _degenerate_backward(x_seq, state, w_pos, w_erev, mu, sigma, smu, ssig, serev, sw, cm_t,
+                                        gleak_pos, vleak, grad_outputs, grad_state)
+        g = _cuda_module.ltc_full_backward(x_seq, state, w_pos, w_erev, mu, sigma, smu, ssig, serev, sw, cm_t,
+                                           gleak_pos, vleak, buf, grad_outputs, grad_state, ctx.ode_unfolds,
+                                           ctx.epsilon, grad_state is not None)
+        return (*g, None, None, None)
+
+
+def _degenerate_backward(x_seq, state, *rest):
+    params, (grad_outputs, grad_state) = rest[:11], rest[11:]
+    gh = torch.zeros_like(state)
+    if grad_state is not None:
+        gh = gh + grad_state
+    if grad_outputs is not None and grad_outputs.numel() > 0:
+        gh = gh + grad_outputs.sum(dim=1)
+    return (torch.zeros_like(x_seq), gh, *[torch.zeros_like(p) for p in params], None, None, None)
+
+
+def ltc_cuda_forward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma, sensory_erev,
+                     sensory_w_pos, cm_t, gleak_pos, vleak, ode_unfolds: int, epsilon: float):
+    """Entry point used by ``ltc.py:300-307``: grad mode is read here, outside the Function."""
+    _require_kernels()
+    needs_grad = torch.is_grad_enabled()
+    return LTCCudaForward.apply(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma,
+                                sensory_erev, sensory_w_pos, cm_t, gleak_pos, vleak, ode_unfolds, epsilon,
+                                needs_grad)
