@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the configuration's global batch (profiling captures of smaller cases)")
     return ap.parse_args()
 
 
@@ -184,6 +186,9 @@ def run_reference(args, cfg, rank):
 def main():
     args = parse()
     cfg = synth.CONFIGS[args.config]
+    if args.batch is not None:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, B=args.batch)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
