@@ -102,6 +102,23 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
                  const float* grad_outputs, const int64_t go_strides[3], const float* grad_state,
                  const LtcGrads* grads, void* workspace, size_t workspace_bytes, ltc_stream_t stream);
 
+/* Size of the fixed device scratch array behind ltc_forward_noalloc (16 MiB per GPU). */
+#define LTC_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* Forward solve that allocates nothing and takes no workspace (no counterpart in
+ * the reference).  For callers that may not allocate GPU memory where they run
+ * the solver -- hosts that own every allocation (a plugin in a serving runtime
+ * with a fixed memory budget) or latency-critical loops in which cudaMalloc
+ * would synchronise the device.  Same inputs and outputs as ltc_forward with
+ * saved == NULL.  Its scratch is one static __device__ array of
+ * LTC_NOALLOC_SCRATCH_BYTES per GPU, held until exit; problems that need more
+ * are rejected with an error.  The first call on a device resolves the array's
+ * address (cudaGetSymbolAddress): make it before any stream capture.  All calls
+ * on a device share the array, so calls that overlap on the GPU race: serialise
+ * them. */
+int ltc_forward_noalloc(const LtcDims* dims, const LtcParams* params, const float* x, const float* h0,
+                        float* outputs, float* h_final, ltc_stream_t stream);
+
 /* Kernel identifiers of the launches each call issues (forward: PACK_FWD,
  * SENSORY_FWD, RECURRENT_FWD; backward: PACK_BWD, RECURRENT_BWD, SENSORY_BWD, FINISH). */
 enum {

@@ -208,6 +208,11 @@ int check_params(const LtcParams* p) {
 
 }  // namespace
 
+namespace ltc {
+// Lets other translation units of the library report through ltc_last_error().
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace ltc
+
 extern "C" {
 
 const char* ltc_last_error(void) { return g_last_error.c_str(); }

@@ -131,6 +131,9 @@ struct FinishArgs {
 };
 cudaError_t launch_finish(const FinishArgs& a, int num_sms, cudaStream_t st);
 
+// Error reporting shared by every extern "C" entry point (ltc_last_error()).
+void set_last_error(const char* msg);
+
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 inline int pad_neurons(int H) { return H <= 32 ? 32 : (H <= 64 ? 64 : round_up(H, 32)); }
 
