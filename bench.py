@@ -32,6 +32,11 @@ import torch.distributed as dist  # noqa: E402
 
 import synth  # noqa: E402
 
+# DRAM bytes per (sample, timestep) of a kernel from one ncu capture of a smaller case
+# of the same configuration (profiles/rec_bwd_fast_c3_b1184.md), scaled to a launch
+# by the (b,t) units it processes.
+NCU_TRAFFIC_PER_BT = {("c3", "recurrent_bwd"): 3535.0}
+
 METRIC = "fwd+bwd sequence-timesteps/sec (B·T/s) at 1/2/4/8 B200; % FP32 roofline"
 UNIT = "B*T/s"
 
@@ -314,7 +319,10 @@ def main():
                    "l2": "256 MB flush write between steps (inside the timed region)"},
         "e2e": e2e,
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": (NCU_TRAFFIC_PER_BT[(cfg.name, dom)] * Bl * cfg.T
+                                 if (cfg.name, dom) in NCU_TRAFFIC_PER_BT else None),
+                     "traffic_unit": "bytes per launch (ncu capture, scaled)",
                      "peak_basis": f"{sms} SMs x 16 MUFU/clk / 2 MUFU per visit at sm_max {f_mhz:.0f} MHz ({peaks_kind})",
                      "step_frac_survey_convention": t_roof / (ms / 1e3)},
         "kernels": kernels,
