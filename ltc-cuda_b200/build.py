@@ -40,11 +40,12 @@ def sources_newer_than_lib() -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
-def build(force: bool = False, verbose_ptxas: bool = False) -> str:
-    if not force and not sources_newer_than_lib():
+def build(force: bool = False, verbose_ptxas: bool = False, out: str = LIB, defines=()) -> str:
+    if out == LIB and not force and not sources_newer_than_lib():
         return LIB
     cmd = [nvcc_path(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "--expt-relaxed-constexpr", "-o", LIB + ".tmp"]
+           "--expt-relaxed-constexpr", "-o", out + ".tmp"]
+    cmd += [f"-D{d}" for d in defines]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     cmd += [os.path.join(CSRC, s) for s in SOURCES]
@@ -55,13 +56,16 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         raise RuntimeError("nvcc failed building libltc_sm100.so")
     if verbose_ptxas:
         sys.stderr.write(r.stderr)
-    os.replace(LIB + ".tmp", LIB)
-    return LIB
+    os.replace(out + ".tmp", out)
+    return out
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--verbose-ptxas", action="store_true")
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--out", default=LIB, help="output path (variant builds for tuning)")
+    ap.add_argument("-D", dest="defines", action="append", default=[], help="extra preprocessor define")
     a = ap.parse_args()
-    print(build(force=a.force or a.verbose_ptxas, verbose_ptxas=a.verbose_ptxas))
+    print(build(force=a.force or a.verbose_ptxas, verbose_ptxas=a.verbose_ptxas, out=os.path.abspath(a.out),
+                defines=a.defines))

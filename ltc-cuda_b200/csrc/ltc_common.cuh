@@ -35,10 +35,39 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// act = sigmoid(sigma * (v - mu)) given the gate pack (sl, nm).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// act = sigmoid(sigma * (v - mu)) given the gate pack (sl, nm): ex2 + rcp (2 MUFU).
 __device__ __forceinline__ float gate(float sl, float nm, float v) {
   return rcp_approx(1.0f + ex2_approx(fmaf(sl, v, nm)));
 }
+
+// Same gate with one MUFU op: the reciprocal 1/(1+e) runs on the FMA pipe as two
+// Newton-Raphson steps r <- r*(2 - d*r) from the classic integer-subtraction seed
+// (bits(r0) = 0x7EF311C7 - bits(d), max relative error 5.1e-2), which leaves a
+// relative error <= 6.7e-6 for every d in [1, 2^64].  y is clamped to 64 so that
+// d stays finite (act < 6e-20 there, i.e. 0 to fp32 accuracy).
+__device__ __forceinline__ float gate_newton(float sl, float nm, float v) {
+  const float d = 1.0f + ex2_approx(fminf(fmaf(sl, v, nm), 64.0f));
+  float r = __int_as_float(0x7EF311C7 - __float_as_int(d));
+  r = r * fmaf(-d, r, 2.0f);
+  r = r * fmaf(-d, r, 2.0f);
+  return r;
+}
+
+// Backward-pass gate with one MUFU op: sigmoid(z) = 0.5 + 0.5*tanh(z/2), given the
+// half-scale pack (sh, nh) = (sigma/2, -sigma*mu/2) so that z/2 = sh*v + nh.
+// tanh.approx has a relative error of about 2^-11; the adjoint tolerates it
+// (gradient bar rtol 5e-2), the forward state does not use it.
+__device__ __forceinline__ float gate_tanh(float sh, float nh, float v) {
+  return fmaf(0.5f, tanh_approx(fmaf(sh, v, nh)), 0.5f);
+}
+// pack (sl, nm) = (-sigma*log2 e, sigma*mu*log2 e)  ->  half-scale pack (sh, nh)
+#define LTC_HALF_SCALE (-0.5f * LTC_LN2)
 
 // ---------------------------------------------------------------------------
 // Transposed reduction across the TPC lanes that share one neuron.

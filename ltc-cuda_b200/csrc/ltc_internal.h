@@ -5,6 +5,12 @@
 #include <stddef.h>
 #include <stdint.h>
 
+// Number of the 8 synapses per thread whose forward gate uses the MUFU reciprocal
+// (the others use the FMA-pipe Newton reciprocal); tuned on B200.
+#ifndef LTC_FWD_MUFU_RCP
+#define LTC_FWD_MUFU_RCP 2
+#endif
+
 namespace ltc {
 
 // ---- parameter packing --------------------------------------------------

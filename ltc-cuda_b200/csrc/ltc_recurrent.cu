@@ -29,6 +29,14 @@ struct Geometry {
   __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (HP / 2) + 4 * g + (j % 4); }
 };
 
+// Gate of synapse j in the forward kernels: synapses j < kMufuRcp use the MUFU
+// reciprocal, the rest the FMA-pipe Newton reciprocal, balancing the two pipes.
+constexpr int kMufuRcp = LTC_FWD_MUFU_RCP;
+
+__device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
+  return j < kMufuRcp ? gate(sl, nm, v) : gate_newton(sl, nm, v);
+}
+
 template <int HP>
 __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a) {
   using G = Geometry<HP>;
@@ -92,7 +100,7 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
           float sn_ = 0.f, sd_ = 0.f;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float act = gate(sl[j], nm[j], v8[j]);
+            const float act = fwd_gate(j, sl[j], nm[j], v8[j]);
             sn_ = fmaf(we[j], act, sn_);
             sd_ = fmaf(wp[j], act, sd_);
           }
@@ -168,7 +176,7 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 pk = a.pack[p * HP + G::sub(j, g)];
-    sl[j] = pk.x; nm[j] = pk.y; wp[j] = pk.z; we[j] = pk.w;
+    sl[j] = pk.x * LTC_HALF_SCALE; nm[j] = pk.y * LTC_HALF_SCALE; wp[j] = pk.z; we[j] = pk.w;
     Gwe[j] = Gwp[j] = Gdz[j] = Gdzv[j] = 0.f;
   }
   const float4 np_ = a.nrn[p];
@@ -270,7 +278,7 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
         float dv = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float act = gate(sl[j], nm[j], vp);
+          const float act = gate_tanh(sl[j], nm[j], vp);
           const float sp = fmaf(-act, act, act);
           const float dz = fmaf(an8[j], we[j], ad8[j] * wp[j]) * sp;
           Gwe[j] = fmaf(an8[j], act, Gwe[j]);
@@ -288,7 +296,7 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
           const int s = blk * kSB + own + o;
           if (s < nvalid) {
             const int idx = s * LDV + p;
-            float gval = DIR[idx] - acc[0][o] * LTC_LN2;  // dL/dv_n[p]
+            float gval = fmaf(2.0f, acc[0][o], DIR[idx]);  // dL/dv_n[p] (sl holds sigma/2)
             const long long bs = b0 + s;
             if (k == 0) {
               const long long row = bs * T + t;

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(512, 1) rec_fwd_wide(RecFwdArgs a) {
           const float4 w = pk[pp * HPW];
 #pragma unroll
           for (int i = 0; i < NSPT; ++i) {
-            const float act = gate(w.x, w.y, vrow[i * HPW + pp]);
+            const float act = gate_newton(w.x, w.y, vrow[i * HPW + pp]);
             accn[i] = fmaf(w.w, act, accn[i]);
             accd[i] = fmaf(w.z, act, accd[i]);
           }
@@ -219,14 +219,15 @@ __global__ void __launch_bounds__(512, 1) rec_bwd_wide(RecBwdArgs a) {
       const float4* pk = pks + (cc & 1) * PC * HPW + p;
       for (int qq = 0; qq < PC; ++qq) {
         const int q = c * PC + qq;
-        const float4 w = pk[qq * HPW];
+        const float4 w0 = pk[qq * HPW];
+        const float4 w = make_float4(w0.x * LTC_HALF_SCALE, w0.y * LTC_HALF_SCALE, w0.z, w0.w);
         float* gp = slab + (long long)q * HPW;
         float g0 = gp[0], g1 = gp[hp2], g2 = gp[2 * hp2], g3 = gp[3 * hp2];
 #pragma unroll
         for (int i = 0; i < NSPT; ++i) {
           const float an = ans[i * HPW + q];
           const float ad = ads[i * HPW + q];
-          const float act = gate(w.x, w.y, vcur[i]);
+          const float act = gate_tanh(w.x, w.y, vcur[i]);
           const float sp = fmaf(-act, act, act);
           const float dz = fmaf(an, w.w, ad * w.z) * sp;
           g0 = fmaf(an, act, g0);
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(512, 1) rec_bwd_wide(RecBwdArgs a) {
 #pragma unroll
     for (int i = 0; i < NSPT; ++i) {
       if (!ok[i]) continue;
-      float gval = dir[i] - dv[i] * LTC_LN2;
+      float gval = fmaf(2.0f, dv[i], dir[i]);
       if (k == 0) {
         const long long row = bs[i] * T + t;
         a.gsn[row * H + p] = gsn[i];

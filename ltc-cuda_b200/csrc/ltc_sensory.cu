@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
         const float xv[kRB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
         for (int r = 0; r < kRB; ++r) {
-          const float act = gate(w.x, w.y, xv[r]);
+          const float act = (r & 1) ? gate_newton(w.x, w.y, xv[r]) : gate(w.x, w.y, xv[r]);
           sn[r] = fmaf(w.w, act, sn[r]);
           sd[r] = fmaf(w.z, act, sd[r]);
         }
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
   for (int j = 0; j < 8; ++j) {
     float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
     if (dvalid) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
-    sl[j] = pk.x; nm[j] = pk.y; sw[j] = pk.z; swe[j] = pk.w;
+    sl[j] = pk.x * LTC_HALF_SCALE; nm[j] = pk.y * LTC_HALF_SCALE; sw[j] = pk.z; swe[j] = pk.w;
     An[j] = Ad[j] = Dz[j] = Dzx[j] = 0.f;
   }
   const int own = LR::own_base(lane);
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
         float dxs = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float act = gate(sl[j], nm[j], xv);
+          const float act = gate_tanh(sl[j], nm[j], xv);
           const float sp = fmaf(-act, act, act);
           const float dz = fmaf(an8[j], swe[j], ad8[j] * sw[j]) * sp;
           An[j] = fmaf(an8[j], act, An[j]);
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
         for (int o = 0; o < LR::OWN; ++o) {
           const int r = blk * kSB + own + o;
           if (r < nr) {
-            const float v = -acc[0][o] * LTC_LN2;
+            const float v = 2.0f * acc[0][o];
             const long long idx = (rt + r) * D + d;
             if (nqc == 1) a.dx[idx] = v;
             else dxpart[qc * ndx + idx] = v;
