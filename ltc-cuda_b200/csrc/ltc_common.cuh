@@ -4,11 +4,12 @@
 // ------------------------------------------------
 // * fp32 everywhere.  Recurrent matrices are (H, H) row-major indexed
 //   [pre p, post q]; sensory matrices are (D, H) indexed [input d, post q].
-// * A sigmoid gate  act = 1 / (1 + exp(-sigma * (v - mu)))  is evaluated as
-//   act = rcp(1 + ex2(y)),  y = sl * v + nm,  with the per-synapse constants
-//   sl = -sigma * log2(e) and nm = sigma * mu * log2(e) precomputed once
-//   ("gate pack").  ex2/rcp are the hardware MUFU approximations (ex2.approx,
-//   rcp.approx), each within 2 ulp, far inside the parity tolerances.
+// * A sigmoid gate  act = 1 / (1 + exp(-sigma * (v - mu)))  is evaluated from a
+//   per-synapse "gate pack" holding the half-scale constants
+//   (sh, nh) = (sigma/2, -sigma*mu/2), so that z/2 = sh*v + nh, as
+//   act = 0.5 + 0.5 * tanh(z/2) with the hardware tanh.approx (one MUFU op).
+//   The forward kernels fold the 0.5 terms into sums of the weights; the
+//   ex2 + reciprocal form (gate / gate_newton below) is kept as a variant.
 // * Saved forward state for the backward pass:
 //     V[n][b][h], n = t*U + k, n in [0, T*U]: the input of unfold k at step t
 //       (V[T*U] is the final state);
@@ -41,7 +42,8 @@ __device__ __forceinline__ float tanh_approx(float x) {
   return y;
 }
 
-// act = sigmoid(sigma * (v - mu)) given the gate pack (sl, nm): ex2 + rcp (2 MUFU).
+// act = sigmoid(sigma * (v - mu)) given the ex2-scale constants
+// (sl, nm) = (-sigma*log2 e, sigma*mu*log2 e): ex2 + rcp (2 MUFU).
 __device__ __forceinline__ float gate(float sl, float nm, float v) {
   return rcp_approx(1.0f + ex2_approx(fmaf(sl, v, nm)));
 }
@@ -66,8 +68,8 @@ __device__ __forceinline__ float gate_newton(float sl, float nm, float v) {
 __device__ __forceinline__ float gate_tanh(float sh, float nh, float v) {
   return fmaf(0.5f, tanh_approx(fmaf(sh, v, nh)), 0.5f);
 }
-// pack (sl, nm) = (-sigma*log2 e, sigma*mu*log2 e)  ->  half-scale pack (sh, nh)
-#define LTC_HALF_SCALE (-0.5f * LTC_LN2)
+// half-scale pack (sh, nh)  ->  ex2-scale (sl, nm) = (-sigma*log2 e, sigma*mu*log2 e)
+#define LTC_EX2_SCALE (-2.0f * LTC_LOG2E)
 
 // ---------------------------------------------------------------------------
 // Transposed reduction across the TPC lanes that share one neuron.

@@ -11,6 +11,14 @@
 #define LTC_FWD_MUFU_RCP 2
 #endif
 
+// 1 (default): the register-resident forward kernel evaluates its gates with one
+// tanh.approx each; 0: ex2 + reciprocal (MUFU / FMA-pipe Newton), kept as a
+// reference variant.  Measured forward error on B200 is ~1e-6 either way (the
+// leak/capacitance term dominates the denominator, so gate errors shrink).
+#ifndef LTC_FWD_TANH
+#define LTC_FWD_TANH 1
+#endif
+
 namespace ltc {
 
 // ---- parameter packing --------------------------------------------------
@@ -26,9 +34,9 @@ struct PackArgs {
   const float* cm;      // (H)
   const float* gl;      // (H)
   const float* vl;      // (H)
-  float4* pack;         // [HP][HP]  (sl, nm, w_pos, w_erev) indexed [p][q]
+  float4* pack;         // [HP][HP]  (sh, nh, w_pos, w_erev) indexed [p][q]
   float4* packT;        // [HP][HP]  same, indexed [q][p]   (may be null)
-  float4* spack;        // [D][HP]   (sl, nm, sw, sw*serev)
+  float4* spack;        // [D][HP]   (sh, nh, sw, sw*serev)
   float4* nrn;          // [HP]      (cm, gl, vl, gl*vl)
   int D, H, HP;
 };

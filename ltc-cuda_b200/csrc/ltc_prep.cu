@@ -5,7 +5,7 @@
 
 namespace ltc {
 
-// Gate packs (sl, nm, w, w*erev) with zero padding up to HP; see ltc_common.cuh.
+// Gate packs (sh, nh, w, w*erev) with zero padding up to HP; see ltc_common.cuh.
 __global__ void pack_kernel(PackArgs a) {
   const long long nrec = (long long)a.HP * a.HP;
   const long long nsen = (long long)a.D * a.HP;
@@ -18,8 +18,8 @@ __global__ void pack_kernel(PackArgs a) {
       if (p < a.H && q < a.H) {
         const long long j = (long long)p * a.H + q;
         const float sg = a.sigma[j];
-        v.x = -sg * LTC_LOG2E;
-        v.y = sg * a.mu[j] * LTC_LOG2E;
+        v.x = 0.5f * sg;
+        v.y = -0.5f * sg * a.mu[j];
         v.z = a.w_pos[j];
         v.w = a.w_erev[j];
       }
@@ -32,8 +32,8 @@ __global__ void pack_kernel(PackArgs a) {
       if (q < a.H) {
         const long long j = (long long)d * a.H + q;
         const float sg = a.ssig[j];
-        v.x = -sg * LTC_LOG2E;
-        v.y = sg * a.smu[j] * LTC_LOG2E;
+        v.x = 0.5f * sg;
+        v.y = -0.5f * sg * a.smu[j];
         v.z = a.sw[j];
         v.w = a.sw[j] * a.serev[j];
       }

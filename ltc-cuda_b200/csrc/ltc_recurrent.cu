@@ -2,16 +2,22 @@
 //
 // One CTA owns a group of `ns` samples for the whole sequence (all T*U
 // unfolds in one launch) and keeps every recurrent synapse of the cell in
-// registers: HP*HP/8 threads, 8 synapses per thread, 4 gate-pack values per
-// synapse (and, in the backward kernel, 4 gradient accumulators per synapse).
-// Per unfold the only traffic is the sample state in shared memory; one
-// __syncthreads() separates unfolds (Jacobi update: every new v is computed
-// from the previous unfold's v, double-buffered -- unlike an in-place update).
+// registers: each thread holds RPT x 8 synapses (RPT = 2 at HP = 64: 256
+// threads x 16 synapses), 4 gate-pack values per synapse and, in the backward
+// kernel, 4 gradient accumulators per synapse.  Per unfold the only traffic is
+// the sample state in shared memory; one __syncthreads() separates unfolds
+// (Jacobi update: every new v is computed from the previous unfold's v,
+// double-buffered -- unlike an in-place update).
 //
-// Forward thread map:  column q = tid / TPC, lane group g = tid % TPC (TPC = HP/8)
-//                      owns presynaptic rows p(j) = (j/4)*(HP/2) + 4g + j%4.
-// Backward thread map: row p = tid / TPC, owns columns q(j) with the same formula.
-// The interleaved p(j)/q(j) make the float4 shared-memory loads bank-conflict free.
+// Forward thread map:  lane group g = tid % TPC (TPC = HP/8 lanes), column group
+//   c = tid / TPC owns the RPT columns q_r = c + r*HP/RPT and presynaptic rows
+//   p(j) = (j/4)*(HP/2) + 4g + j%4 (j < 8).  The 8 operand loads per sample are
+//   shared by the RPT columns.
+// Backward thread map: row group c owns rows p_r = c + r*HP/RPT and columns q(j).
+// The interleaved p(j)/q(j) make the float4 shared-memory loads bank-conflict
+// free.  Per block of kSB samples, RPT*kSB partial sums are reduced across the
+// TPC lanes by a transposed (recursive-halving) reduction after which every lane
+// owns one (neuron, sample) item and runs its per-neuron "tail".
 #include "ltc_common.cuh"
 #include "ltc_internal.h"
 
@@ -23,9 +29,12 @@ constexpr int kSB = 4;  // samples per register block
 
 template <int HP>
 struct Geometry {
-  static constexpr int TPC = HP / 8;
-  static constexpr int NT = HP * TPC;
-  static constexpr int LDV = HP + 4;  // padded row stride of per-sample vectors
+  static constexpr int RPT = HP >= 64 ? 2 : 1;  // neurons (rows / columns) per thread
+  static constexpr int TPC = HP / 8;            // lanes sharing a neuron group
+  static constexpr int NG = HP / RPT;           // neuron groups
+  static constexpr int NT = NG * TPC;           // threads
+  static constexpr int NI = RPT * kSB;          // reduced items per block
+  static constexpr int LDV = HP + 4;            // padded row stride of per-sample vectors
   __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (HP / 2) + 4 * g + (j % 4); }
 };
 
@@ -40,8 +49,8 @@ __device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
 template <int HP>
 __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a) {
   using G = Geometry<HP>;
-  constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV;
-  using LR = LaneReduce<TPC, kSB>;
+  constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV, RPT = G::RPT, NG = G::NG;
+  using LR = LaneReduce<TPC, G::NI>;
   extern __shared__ __align__(16) float smem[];
   const int ns = a.ns;
   float* vbuf = smem;                // [2][ns][LDV]
@@ -49,22 +58,49 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
   float* sdb = snb + ns * LDV;       // [ns][LDV]
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int q = tid / TPC, g = tid % TPC;
+  const int c = tid / TPC, g = tid % TPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
   const int b0 = blockIdx.x * ns;
   const int nvalid = min(ns, B - b0);
   const int nblk = (nvalid + kSB - 1) / kSB;
 
-  float sl[8], nm[8], wp[8], we[8];
+  float sl[RPT][8], nm[RPT][8], wp[RPT][8], we[RPT][8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 pk = a.pack[G::sub(j, g) * HP + q];
-    sl[j] = pk.x; nm[j] = pk.y; wp[j] = pk.z; we[j] = pk.w;
+  for (int r = 0; r < RPT; ++r)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 pk = a.pack[G::sub(j, g) * HP + c + r * NG];
+      sl[r][j] = pk.x; nm[r][j] = pk.y; wp[r][j] = pk.z; we[r][j] = pk.w;
+    }
+#if !LTC_FWD_TANH
+#pragma unroll
+  for (int r = 0; r < RPT; ++r)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {  // half-scale pack -> ex2-scale pack
+      sl[r][j] *= LTC_EX2_SCALE;
+      nm[r][j] *= LTC_EX2_SCALE;
+    }
+#else
+  float cwe[RPT], cwp[RPT];
+#pragma unroll
+  for (int r = 0; r < RPT; ++r) {
+    cwe[r] = cwp[r] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      we[r][j] *= 0.5f;
+      wp[r][j] *= 0.5f;
+      cwe[r] += we[r][j];
+      cwp[r] += wp[r][j];
+    }
   }
+#endif
+  // the one (column, sample-in-block) item this lane finishes
+  const int own = LR::own_base(lane);
+  const int orow = own / kSB, osmp = own % kSB;
+  const int q = c + orow * NG;
   const float4 nq = a.nrn[q];
   const float cm = nq.x, cmgl = nq.x + nq.y, glvl = nq.w;
   const bool qvalid = q < H;
-  const int own = LR::own_base(lane);
   const bool writer = LR::writer(lane);
 
   for (int i = tid; i < 4 * ns * LDV; i += NT) smem[i] = 0.f;
@@ -90,42 +126,54 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
       const float* vc = vbuf + cur * ns * LDV;
       float* vn = vbuf + (cur ^ 1) * ns * LDV;
       for (int blk = 0; blk < nblk; ++blk) {
-        float acc[2][kSB];
+        float acc[2][G::NI];
 #pragma unroll
         for (int i = 0; i < kSB; ++i) {
           const float* vr = vc + (blk * kSB + i) * LDV + 4 * g;
           const float4 va = *reinterpret_cast<const float4*>(vr);
           const float4 vb = *reinterpret_cast<const float4*>(vr + HP / 2);
           const float v8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-          float sn_ = 0.f, sd_ = 0.f;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float act = fwd_gate(j, sl[j], nm[j], v8[j]);
-            sn_ = fmaf(we[j], act, sn_);
-            sd_ = fmaf(wp[j], act, sd_);
+          for (int r = 0; r < RPT; ++r) {
+#if LTC_FWD_TANH
+            // act = 0.5 + 0.5*tanh(z/2): the constant halves are folded into
+            // cwe/cwp, the weights into the half-scale registers.
+            float sn_ = cwe[r], sd_ = cwp[r];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float th = tanh_approx(fmaf(sl[r][j], v8[j], nm[r][j]));
+              sn_ = fmaf(we[r][j], th, sn_);
+              sd_ = fmaf(wp[r][j], th, sd_);
+            }
+#else
+            float sn_ = 0.f, sd_ = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float act = fwd_gate(j, sl[r][j], nm[r][j], v8[j]);
+              sn_ = fmaf(we[r][j], act, sn_);
+              sd_ = fmaf(wp[r][j], act, sd_);
+            }
+#endif
+            acc[0][r * kSB + i] = sn_;
+            acc[1][r * kSB + i] = sd_;
           }
-          acc[0][i] = sn_;
-          acc[1][i] = sd_;
         }
         LR::template run<2>(acc, lane);
-#pragma unroll
-        for (int o = 0; o < LR::OWN; ++o) {
-          const int s = blk * kSB + own + o;
-          const float v = vc[s * LDV + q];
-          const float wn = acc[0][o] + snb[s * LDV + q];
-          const float wd = acc[1][o] + sdb[s * LDV + q];
-          const float num = (cm * v + glvl) + wn;
-          const float r = rcp_approx((cmgl + wd) + a.eps);
-          const float vnew = num * r;
-          if (qvalid && writer && s < nvalid) {
-            vn[s * LDV + q] = vnew;
-            const long long bs = b0 + s;
-            if (a.V) {
-              a.V[(n * B + bs) * H + q] = v;
-              a.R[(n * B + bs) * H + q] = r;
-            }
-            if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
+        const int s = blk * kSB + osmp;
+        const float v = vc[s * LDV + q];
+        const float wn = acc[0][0] + snb[s * LDV + q];
+        const float wd = acc[1][0] + sdb[s * LDV + q];
+        const float num = (cm * v + glvl) + wn;
+        const float rr = rcp_approx((cmgl + wd) + a.eps);
+        const float vnew = num * rr;
+        if (qvalid && writer && s < nvalid) {
+          vn[s * LDV + q] = vnew;
+          const long long bs = b0 + s;
+          if (a.V) {
+            a.V[(n * B + bs) * H + q] = v;
+            a.R[(n * B + bs) * H + q] = rr;
           }
+          if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
         }
       }
       __syncthreads();
@@ -150,8 +198,8 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
 template <int HP>
 __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a) {
   using G = Geometry<HP>;
-  constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV;
-  using LR = LaneReduce<TPC, kSB>;
+  constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV, RPT = G::RPT, NG = G::NG;
+  using LR = LaneReduce<TPC, G::NI>;
   extern __shared__ __align__(16) float smem[];
   const int ns = a.ns;
   const int SL = ns * LDV;  // one per-sample slab
@@ -161,28 +209,34 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   float* RS = VS + 3 * SL;   // [2]
   float* DIR = RS + 2 * SL;
   float* GSN = DIR + SL;
-  float* GSD = GSN + SL;     // total 13 slabs
+  float* GSD = GSN + SL;     // 13 slabs, then [3][HP][TPC] for the final per-neuron sums
+  float* red = GSD + SL;
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int p = tid / TPC, g = tid % TPC;
+  const int c = tid / TPC, g = tid % TPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
   const int b0 = blockIdx.x * ns;
   const int nvalid = min(ns, B - b0);
   const int nblk = (nvalid + kSB - 1) / kSB;
   const long long NTU = (long long)T * U;
 
-  float sl[8], nm[8], wp[8], we[8];
-  float Gwe[8], Gwp[8], Gdz[8], Gdzv[8];
+  float sl[RPT][8], nm[RPT][8], wp[RPT][8], we[RPT][8];
+  float Gwe[RPT][8], Gwp[RPT][8], Gdz[RPT][8], Gdzv[RPT][8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 pk = a.pack[p * HP + G::sub(j, g)];
-    sl[j] = pk.x * LTC_HALF_SCALE; nm[j] = pk.y * LTC_HALF_SCALE; wp[j] = pk.z; we[j] = pk.w;
-    Gwe[j] = Gwp[j] = Gdz[j] = Gdzv[j] = 0.f;
-  }
+  for (int r = 0; r < RPT; ++r)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 pk = a.pack[(c + r * NG) * HP + G::sub(j, g)];
+      sl[r][j] = pk.x; nm[r][j] = pk.y; wp[r][j] = pk.z; we[r][j] = pk.w;
+      Gwe[r][j] = Gwp[r][j] = Gdz[r][j] = Gdzv[r][j] = 0.f;
+    }
+  // the one (row, sample-in-block) item this lane finishes
+  const int own = LR::own_base(lane);
+  const int orow = own / kSB, osmp = own % kSB;
+  const int p = c + orow * NG;
   const float4 np_ = a.nrn[p];
   const float cm = np_.x, gl = np_.y, vl = np_.z;
   const bool pvalid = p < H;
-  const int own = LR::own_base(lane);
   const bool writer = LR::writer(lane);
   float gcm = 0.f, ggl = 0.f, gvl = 0.f;
 
@@ -230,17 +284,14 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   };
 
   // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate
-  if (pvalid) {
+  if (pvalid && writer) {
     for (int blk = 0; blk < nblk; ++blk) {
-#pragma unroll
-      for (int o = 0; o < LR::OWN; ++o) {
-        const int s = blk * kSB + own + o;
-        if (writer && s < nvalid) {
-          const long long bs = b0 + s;
-          float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
-          if (a.gstate) gval += a.gstate[bs * H + p];
-          prep(NTU - 1, s, gval, true);
-        }
+      const int s = blk * kSB + osmp;
+      if (s < nvalid) {
+        const long long bs = b0 + s;
+        float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
+        if (a.gstate) gval += a.gstate[bs * H + p];
+        prep(NTU - 1, s, gval, true);
       }
     }
   }
@@ -262,11 +313,10 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
     const float* vsn = VS + (int)(n % 3) * SL;
     const int t = (int)(n / U), k = (int)(n % U);
     for (int blk = 0; blk < nblk; ++blk) {
-      float acc[1][kSB];
+      float acc[1][G::NI];
 #pragma unroll
       for (int i = 0; i < kSB; ++i) {
         const int s = blk * kSB + i;
-        const float vp = vsn[s * LDV + p];
         const float* ar = an_s + s * LDV + 4 * g;
         const float* dr = ad_s + s * LDV + 4 * g;
         const float4 a0 = *reinterpret_cast<const float4*>(ar);
@@ -275,42 +325,43 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
         const float4 d1 = *reinterpret_cast<const float4*>(dr + HP / 2);
         const float an8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         const float ad8[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-        float dv = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float act = gate_tanh(sl[j], nm[j], vp);
-          const float sp = fmaf(-act, act, act);
-          const float dz = fmaf(an8[j], we[j], ad8[j] * wp[j]) * sp;
-          Gwe[j] = fmaf(an8[j], act, Gwe[j]);
-          Gwp[j] = fmaf(ad8[j], act, Gwp[j]);
-          Gdz[j] += dz;
-          Gdzv[j] = fmaf(dz, vp, Gdzv[j]);
-          dv = fmaf(dz, sl[j], dv);
+        for (int r = 0; r < RPT; ++r) {
+          const float vp = vsn[s * LDV + c + r * NG];
+          float dv = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float act = gate_tanh(sl[r][j], nm[r][j], vp);
+            const float sp = fmaf(-act, act, act);
+            const float dz = fmaf(an8[j], we[r][j], ad8[j] * wp[r][j]) * sp;
+            Gwe[r][j] = fmaf(an8[j], act, Gwe[r][j]);
+            Gwp[r][j] = fmaf(ad8[j], act, Gwp[r][j]);
+            Gdz[r][j] += dz;
+            Gdzv[r][j] = fmaf(dz, vp, Gdzv[r][j]);
+            dv = fmaf(dz, sl[r][j], dv);
+          }
+          acc[0][r * kSB + i] = dv;
         }
-        acc[0][i] = dv;
       }
       LR::template run<1>(acc, lane);
-      if (pvalid && writer) {
-#pragma unroll
-        for (int o = 0; o < LR::OWN; ++o) {
-          const int s = blk * kSB + own + o;
-          if (s < nvalid) {
-            const int idx = s * LDV + p;
-            float gval = fmaf(2.0f, acc[0][o], DIR[idx]);  // dL/dv_n[p] (sl holds sigma/2)
-            const long long bs = b0 + s;
-            if (k == 0) {
-              const long long row = bs * T + t;
-              a.gsn[row * H + p] = GSN[idx];
-              a.gsd[row * H + p] = GSD[idx];
-              if (t == 0) {
-                a.gh0[bs * H + p] = gval;
-                continue;
-              }
-              gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
-            }
-            prep(n - 1, s, gval, k == 0);
+      const int s = blk * kSB + osmp;
+      if (pvalid && writer && s < nvalid) {
+        const int idx = s * LDV + p;
+        float gval = fmaf(2.0f, acc[0][0], DIR[idx]);  // dL/dv_n[p] (sl holds sigma/2)
+        const long long bs = b0 + s;
+        bool done = false;
+        if (k == 0) {
+          const long long row = bs * T + t;
+          a.gsn[row * H + p] = GSN[idx];
+          a.gsd[row * H + p] = GSD[idx];
+          if (t == 0) {
+            a.gh0[bs * H + p] = gval;
+            done = true;
+          } else {
+            gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
           }
         }
+        if (!done) prep(n - 1, s, gval, k == 0);
       }
     }
     cp_async_wait_all();
@@ -320,24 +371,33 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   // partial gradients of this CTA
   float* part = a.part + (long long)blockIdx.x * 4 * HP * HP;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int idx = p * HP + G::sub(j, g);
-    part[idx] = Gwe[j];
-    part[HP * HP + idx] = Gwp[j];
-    part[2 * HP * HP + idx] = Gdz[j];
-    part[3 * HP * HP + idx] = Gdzv[j];
-  }
+  for (int r = 0; r < RPT; ++r)
 #pragma unroll
-  for (int stride = TPC / 2; stride >= 1; stride >>= 1) {
-    gcm += __shfl_xor_sync(0xffffffffu, gcm, stride);
-    ggl += __shfl_xor_sync(0xffffffffu, ggl, stride);
-    gvl += __shfl_xor_sync(0xffffffffu, gvl, stride);
+    for (int j = 0; j < 8; ++j) {
+      const int idx = (c + r * NG) * HP + G::sub(j, g);
+      part[idx] = Gwe[r][j];
+      part[HP * HP + idx] = Gwp[r][j];
+      part[2 * HP * HP + idx] = Gdz[r][j];
+      part[3 * HP * HP + idx] = Gdzv[r][j];
+    }
+  // per-neuron sums: each lane holds the partial of its own row; fixed-order sum
+  // over the lanes of the group through shared memory.
+  for (int i = tid; i < 3 * HP * TPC; i += NT) red[i] = 0.f;
+  __syncthreads();
+  if (writer) {
+    red[(0 * HP + p) * TPC + g] = gcm;
+    red[(1 * HP + p) * TPC + g] = ggl;
+    red[(2 * HP + p) * TPC + g] = gvl;
   }
-  if (g == 0) {
+  __syncthreads();
+  if (tid < HP) {
     float* pn = a.partn + (long long)blockIdx.x * 3 * HP;
-    pn[p] = gcm;
-    pn[HP + p] = ggl;
-    pn[2 * HP + p] = gvl;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float sum = 0.f;
+      for (int l = 0; l < TPC; ++l) sum += red[(k * HP + tid) * TPC + l];
+      pn[k * HP + tid] = sum;
+    }
   }
 }
 
@@ -384,10 +444,10 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   if (per < 1) per = 1;
   p.ns_fwd = p.ns_bwd = per * kSB;
   p.grid_fwd = p.grid_bwd = (B + p.ns_fwd - 1) / p.ns_fwd;
-  p.threads_fwd = p.threads_bwd = HP * HP / 8;
+  p.threads_fwd = p.threads_bwd = HP == 32 ? 128 : 256;
   p.slots_bwd = p.grid_bwd;
   p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
-  p.smem_bwd = (size_t)13 * p.ns_bwd * LDV * sizeof(float);
+  p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 3 * HP * (HP / 8)) * sizeof(float);
   return p;
 }
 

@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(512, 1) rec_fwd_wide(RecFwdArgs a) {
       const long long n = (long long)t * U + u;
       const float* vc = vbuf + cur * ns * HPW;
       float* vn = vbuf + (cur ^ 1) * ns * HPW;
-      float accn[NSPT], accd[NSPT];
+      // act = 0.5 + 0.5*tanh(z/2): accumulate sum w*tanh and add sum w at the end
+      float accn[NSPT], accd[NSPT], cwe = 0.f, cwp = 0.f;
 #pragma unroll
       for (int i = 0; i < NSPT; ++i) accn[i] = accd[i] = 0.f;
       for (int c = 0; c < NC; ++c, ++cc) {
@@ -82,11 +83,13 @@ __global__ void __launch_bounds__(512, 1) rec_fwd_wide(RecFwdArgs a) {
         const float* vrow = vc + (sg * NSPT) * HPW + c * PC;
         for (int pp = 0; pp < PC; ++pp) {
           const float4 w = pk[pp * HPW];
+          cwe += w.w;
+          cwp += w.z;
 #pragma unroll
           for (int i = 0; i < NSPT; ++i) {
-            const float act = gate_newton(w.x, w.y, vrow[i * HPW + pp]);
-            accn[i] = fmaf(w.w, act, accn[i]);
-            accd[i] = fmaf(w.z, act, accd[i]);
+            const float th = tanh_approx(fmaf(w.x, vrow[i * HPW + pp], w.y));
+            accn[i] = fmaf(w.w, th, accn[i]);
+            accd[i] = fmaf(w.z, th, accd[i]);
           }
         }
       }
@@ -94,8 +97,8 @@ __global__ void __launch_bounds__(512, 1) rec_fwd_wide(RecFwdArgs a) {
       for (int i = 0; i < NSPT; ++i) {
         const int s = sg * NSPT + i;
         const float v = vc[s * HPW + q];
-        const float num = (cm * v + glvl) + (accn[i] + snt[s * HPW + q]);
-        const float r = rcp_approx((cmgl + (accd[i] + sdt[s * HPW + q])) + a.eps);
+        const float num = (cm * v + glvl) + (0.5f * (cwe + accn[i]) + snt[s * HPW + q]);
+        const float r = rcp_approx((cmgl + (0.5f * (cwp + accd[i]) + sdt[s * HPW + q])) + a.eps);
         const float vnew = num * r;
         if (q < H && s < nvalid) {
           vn[s * HPW + q] = vnew;
@@ -219,8 +222,7 @@ __global__ void __launch_bounds__(512, 1) rec_bwd_wide(RecBwdArgs a) {
       const float4* pk = pks + (cc & 1) * PC * HPW + p;
       for (int qq = 0; qq < PC; ++qq) {
         const int q = c * PC + qq;
-        const float4 w0 = pk[qq * HPW];
-        const float4 w = make_float4(w0.x * LTC_HALF_SCALE, w0.y * LTC_HALF_SCALE, w0.z, w0.w);
+        const float4 w = pk[qq * HPW];
         float* gp = slab + (long long)q * HPW;
         float g0 = gp[0], g1 = gp[hp2], g2 = gp[2 * hp2], g3 = gp[3 * hp2];
 #pragma unroll

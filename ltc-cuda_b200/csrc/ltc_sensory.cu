@@ -51,7 +51,8 @@ __global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
   const long long ntiles = (a.rows + G.TR - 1) / G.TR;
   for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const long long row0 = tile * G.TR;
-    float sn[kRB], sd[kRB];
+    // act = 0.5 + 0.5*tanh(z/2): accumulate sum w*tanh, add sum w at the end
+    float sn[kRB], sd[kRB], csw = 0.f, cswe = 0.f;
 #pragma unroll
     for (int r = 0; r < kRB; ++r) sn[r] = sd[r] = 0.f;
     for (int d0 = 0; d0 < D; d0 += G.DC) {
@@ -67,14 +68,16 @@ __global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
       const float* xr = xs + rg * kRB;
       for (int dd = 0; dd < dc; ++dd) {
         const float4 w = pks[dd * G.HPW + q];
+        cswe += w.w;
+        csw += w.z;
         const float4 x0 = *reinterpret_cast<const float4*>(xr + dd * G.TR);
         const float4 x1 = *reinterpret_cast<const float4*>(xr + dd * G.TR + 4);
         const float xv[kRB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
         for (int r = 0; r < kRB; ++r) {
-          const float act = (r & 1) ? gate_newton(w.x, w.y, xv[r]) : gate(w.x, w.y, xv[r]);
-          sn[r] = fmaf(w.w, act, sn[r]);
-          sd[r] = fmaf(w.z, act, sd[r]);
+          const float th = tanh_approx(fmaf(w.x, xv[r], w.y));
+          sn[r] = fmaf(w.w, th, sn[r]);
+          sd[r] = fmaf(w.z, th, sd[r]);
         }
       }
     }
@@ -83,8 +86,8 @@ __global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
       for (int r = 0; r < kRB; ++r) {
         const long long row = row0 + rg * kRB + r;
         if (row < a.rows) {
-          a.sn[row * H + q] = sn[r];
-          a.sd[row * H + q] = sd[r];
+          a.sn[row * H + q] = 0.5f * (cswe + sn[r]);
+          a.sd[row * H + q] = 0.5f * (csw + sd[r]);
         }
       }
     }
@@ -124,7 +127,7 @@ __global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
   for (int j = 0; j < 8; ++j) {
     float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
     if (dvalid) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
-    sl[j] = pk.x * LTC_HALF_SCALE; nm[j] = pk.y * LTC_HALF_SCALE; sw[j] = pk.z; swe[j] = pk.w;
+    sl[j] = pk.x; nm[j] = pk.y; sw[j] = pk.z; swe[j] = pk.w;
     An[j] = Ad[j] = Dz[j] = Dzx[j] = 0.f;
   }
   const int own = LR::own_base(lane);
