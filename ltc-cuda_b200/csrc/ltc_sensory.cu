@@ -8,7 +8,7 @@
 // Forward: thread = (column q, row group rg), RB rows per thread, no
 //   cross-thread reduction; the gate pack of a chunk of DC inputs and the x
 //   tile are staged in shared memory and shared by the row groups.
-// Backward: thread = (input d, lane group g) owning 8 columns of a QC-column
+// Backward: thread = (2 inputs d, lane group g) owning 8 columns of a QC-column
 //   chunk (the same map as the recurrent backward kernel with p -> d); it
 //   accumulates the 4 synapse-gradient sums in registers over all rows of its
 //   row split and writes them once; dx[row][d] is reduced over the TPC lanes.
@@ -96,40 +96,47 @@ __global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
 
 template <int QC>
 struct SensBwdGeom {
-  static constexpr int TPC = QC / 8;
-  static constexpr int DPC = 4096 / QC;  // inputs per CTA (512 threads)
+  static constexpr int NT = 256;         // threads
+  static constexpr int TPC = QC / 8;     // lanes sharing an input pair
+  static constexpr int NGD = NT / TPC;   // input groups; each thread owns 2 inputs
+  static constexpr int DPC = 2 * NGD;    // inputs per CTA (= 4096 / QC)
   static constexpr int LDG = QC + 4;
   __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (QC / 2) + 4 * g + (j % 4); }
 };
 
+// Thread = (input pair c, lane g): inputs d_r = d0 + c + r*NGD (r < 2), columns
+// q0 + sub(j, g).  The per-row adjoint loads (8 columns of gsn, gsd) are shared
+// by the two inputs.
 template <int QC>
-__global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc, long long rows_per_split,
+__global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc, long long rows_per_split,
                                                           float* dxpart) {
   using G = SensBwdGeom<QC>;
-  constexpr int TPC = G::TPC, DPC = G::DPC, LDG = G::LDG;
-  using LR = LaneReduce<TPC, kSB>;
+  constexpr int TPC = G::TPC, DPC = G::DPC, LDG = G::LDG, NT = G::NT, NGD = G::NGD;
+  constexpr int NI = 2 * kSB;
+  using LR = LaneReduce<TPC, NI>;
   extern __shared__ __align__(16) float smem[];
   float* GN = smem;               // [kRT][LDG]
   float* GD = GN + kRT * LDG;     // [kRT][LDG]
   float* XS = GD + kRT * LDG;     // [kRT][DPC]
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int dl = tid / TPC, g = tid % TPC;
+  const int c = tid / TPC, g = tid % TPC;
   const int dchunk = blockIdx.x / nqc, qc = blockIdx.x % nqc;
   const int d0 = dchunk * DPC, q0 = qc * QC;
-  const int d = d0 + dl;
   const int D = a.D, H = a.H, HP = a.HP;
-  const bool dvalid = d < D;
 
-  float sl[8], nm[8], sw[8], swe[8];
-  float An[8], Ad[8], Dz[8], Dzx[8];
+  float sl[2][8], nm[2][8], sw[2][8], swe[2][8];
+  float An[2][8], Ad[2][8], Dz[2][8], Dzx[2][8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (dvalid) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
-    sl[j] = pk.x; nm[j] = pk.y; sw[j] = pk.z; swe[j] = pk.w;
-    An[j] = Ad[j] = Dz[j] = Dzx[j] = 0.f;
-  }
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = d0 + c + r * NGD;
+      float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (d < D) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
+      sl[r][j] = pk.x; nm[r][j] = pk.y; sw[r][j] = pk.z; swe[r][j] = pk.w;
+      An[r][j] = Ad[r][j] = Dz[r][j] = Dzx[r][j] = 0.f;
+    }
   const int own = LR::own_base(lane);
   const bool writer = LR::writer(lane);
   const int hq = min(QC, H - q0);  // valid columns of this chunk
@@ -140,55 +147,60 @@ __global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
   for (long long rt = r_begin; rt < r_end; rt += kRT) {
     const int nr = (int)min((long long)kRT, r_end - rt);
     __syncthreads();
-    for (int i = tid; i < kRT * QC; i += 512) {
-      const int r = i / QC, c = i % QC;
-      const bool ok = r < nr && c < hq;
-      const long long src = (rt + r) * H + q0 + c;
-      GN[r * LDG + c] = ok ? a.gsn[src] : 0.f;
-      GD[r * LDG + c] = ok ? a.gsd[src] : 0.f;
+    for (int i = tid; i < kRT * QC; i += NT) {
+      const int r = i / QC, cc = i % QC;
+      const bool ok = r < nr && cc < hq;
+      const long long src = (rt + r) * H + q0 + cc;
+      GN[r * LDG + cc] = ok ? a.gsn[src] : 0.f;
+      GD[r * LDG + cc] = ok ? a.gsd[src] : 0.f;
     }
-    for (int i = tid; i < kRT * DPC; i += 512) {
-      const int r = i / DPC, c = i % DPC;
-      XS[i] = (r < nr && d0 + c < D) ? a.x[(rt + r) * D + d0 + c] : 0.f;
+    for (int i = tid; i < kRT * DPC; i += NT) {
+      const int r = i / DPC, cc = i % DPC;
+      XS[i] = (r < nr && d0 + cc < D) ? a.x[(rt + r) * D + d0 + cc] : 0.f;
     }
     __syncthreads();
     const int nblk = (nr + kSB - 1) / kSB;
     for (int blk = 0; blk < nblk; ++blk) {
-      float acc[1][kSB];
+      float acc[1][NI];
 #pragma unroll
       for (int i = 0; i < kSB; ++i) {
-        const int r = blk * kSB + i;
-        const float xv = XS[r * DPC + dl];
-        const float* ar = GN + r * LDG + 4 * g;
-        const float* dr = GD + r * LDG + 4 * g;
+        const int row = blk * kSB + i;
+        const float* ar = GN + row * LDG + 4 * g;
+        const float* dr = GD + row * LDG + 4 * g;
         const float4 a0 = *reinterpret_cast<const float4*>(ar);
         const float4 a1 = *reinterpret_cast<const float4*>(ar + QC / 2);
         const float4 e0 = *reinterpret_cast<const float4*>(dr);
         const float4 e1 = *reinterpret_cast<const float4*>(dr + QC / 2);
         const float an8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         const float ad8[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
-        float dxs = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float act = gate_tanh(sl[j], nm[j], xv);
-          const float sp = fmaf(-act, act, act);
-          const float dz = fmaf(an8[j], swe[j], ad8[j] * sw[j]) * sp;
-          An[j] = fmaf(an8[j], act, An[j]);
-          Ad[j] = fmaf(ad8[j], act, Ad[j]);
-          Dz[j] += dz;
-          Dzx[j] = fmaf(dz, xv, Dzx[j]);
-          dxs = fmaf(dz, sl[j], dxs);
+        for (int r = 0; r < 2; ++r) {
+          const float xv = XS[row * DPC + c + r * NGD];
+          float dxs = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float act = gate_tanh(sl[r][j], nm[r][j], xv);
+            const float sp = fmaf(-act, act, act);
+            const float dz = fmaf(an8[j], swe[r][j], ad8[j] * sw[r][j]) * sp;
+            An[r][j] = fmaf(an8[j], act, An[r][j]);
+            Ad[r][j] = fmaf(ad8[j], act, Ad[r][j]);
+            Dz[r][j] += dz;
+            Dzx[r][j] = fmaf(dz, xv, Dzx[r][j]);
+            dxs = fmaf(dz, sl[r][j], dxs);
+          }
+          acc[0][r * kSB + i] = dxs;
         }
-        acc[0][i] = dxs;
       }
       LR::template run<1>(acc, lane);
-      if (dvalid && writer) {
+      if (writer) {
 #pragma unroll
         for (int o = 0; o < LR::OWN; ++o) {
-          const int r = blk * kSB + own + o;
-          if (r < nr) {
-            const float v = 2.0f * acc[0][o];
-            const long long idx = (rt + r) * D + d;
+          const int item = own + o;
+          const int row = blk * kSB + item % kSB;
+          const int d = d0 + c + (item / kSB) * NGD;
+          if (row < nr && d < D) {
+            const float v = 2.0f * acc[0][o];  // sl holds sigma/2
+            const long long idx = (rt + row) * D + d;
             if (nqc == 1) a.dx[idx] = v;
             else dxpart[qc * ndx + idx] = v;
           }
@@ -196,16 +208,19 @@ __global__ void __launch_bounds__(512, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
       }
     }
   }
-  if (dvalid) {
-    const long long slab = (long long)D * HP;
+  const long long slab = (long long)D * HP;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int d = d0 + c + r * NGD;
+    if (d >= D) continue;
     float* part = a.part + (long long)blockIdx.y * 4 * slab + (long long)d * HP + q0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int c = G::sub(j, g);
-      part[c] = An[j];
-      part[slab + c] = Ad[j];
-      part[2 * slab + c] = Dz[j];
-      part[3 * slab + c] = Dzx[j];
+      const int cc = G::sub(j, g);
+      part[cc] = An[r][j];
+      part[slab + cc] = Ad[r][j];
+      part[2 * slab + cc] = Dz[r][j];
+      part[3 * slab + cc] = Dzx[r][j];
     }
   }
 }
@@ -259,7 +274,7 @@ cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float
     e = cudaFuncSetAttribute(sens_bwd_kernel<QCV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                              (int)smem);                                                         \
     if (e != cudaSuccess) return e;                                                               \
-    sens_bwd_kernel<QCV><<<grid, 512, smem, st>>>(a, p.nqc, rps, dxpart);                         \
+    sens_bwd_kernel<QCV><<<grid, 256, smem, st>>>(a, p.nqc, rps, dxpart);                         \
     break;
   switch (p.qc) {
     LTC_SB_CASE(32)
