@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   const int b0 = blockIdx.x * ns;
   const int nvalid = min(ns, B - b0);
   const int nblk = (nvalid + kSB - 1) / kSB;
-  const long long NTU = (long long)T * U;
+  const int NTU = T * U;  // unfolds in the sequence
 
   float sl[RPT][8], nm[RPT][8], wp[RPT][8], we[RPT][8];
   float Gwe[RPT][8], Gwp[RPT][8], Gdz[RPT][8], Gdzv[RPT][8];
@@ -244,14 +244,14 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   __syncthreads();
 
   // stage saved slices: V[m] -> VS[m%3], R[m] -> RS[m%2]
-  auto stage_v = [&](long long m) {
-    float* dst = VS + (int)(m % 3) * SL;
-    const float* src = a.V + m * B * H + (long long)b0 * H;
+  auto stage_v = [&](int m) {
+    float* dst = VS + (m % 3) * SL;
+    const float* src = a.V + ((long long)m * B + b0) * H;
     for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
   };
-  auto stage_r = [&](long long m) {
-    float* dst = RS + (int)(m % 2) * SL;
-    const float* src = a.R + m * B * H + (long long)b0 * H;
+  auto stage_r = [&](int m) {
+    float* dst = RS + (m % 2) * SL;
+    const float* src = a.R + ((long long)m * B + b0) * H;
     for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
   };
   stage_v(NTU);
@@ -265,22 +265,25 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   cp_async_wait_all();
   __syncthreads();
 
-  // Per-neuron prep of unfold m for (sample s, neuron p) given g = dL/dv_{m+1}[p].
-  auto prep = [&](long long m, int s, float gval, bool first_of_step) {
-    const float r = RS[(int)(m % 2) * SL + s * LDV + p];
-    const float vin = VS[(int)(m % 3) * SL + s * LDV + p];
-    const float vout = VS[(int)((m + 1) % 3) * SL + s * LDV + p];
+  // Per-neuron prep of unfold m for (sample s, neuron p) given g = dL/dv_{m+1}[p]:
+  // rs/vin/vout/an/ad point at the slabs of R[m], V[m], V[m+1] and the adjoint
+  // slabs of unfold m (slot arithmetic done once per unfold by the caller).
+  auto prep = [&](const float* rs, const float* vin_s, const float* vout_s, float* an_d, float* ad_d, int s,
+                  float gval, bool first_of_step) {
+    const int idx = s * LDV + p;
+    const float r = rs[idx];
+    const float vin = vin_s[idx];
+    const float vout = vout_s[idx];
     const float an = gval * r;
     const float ad = -an * vout;
     gcm = fmaf(an, vin - vout, gcm);
     ggl = fmaf(an, vl - vout, ggl);
     gvl = fmaf(an, gl, gvl);
-    const int idx = s * LDV + p;
     GSN[idx] = first_of_step ? an : GSN[idx] + an;
     GSD[idx] = first_of_step ? ad : GSD[idx] + ad;
     DIR[idx] = an * cm;
-    AN[(int)(m % 2) * SL + idx] = an;
-    AD[(int)(m % 2) * SL + idx] = ad;
+    an_d[idx] = an;
+    ad_d[idx] = ad;
   };
 
   // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate
@@ -291,13 +294,16 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
         const long long bs = b0 + s;
         float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
         if (a.gstate) gval += a.gstate[bs * H + p];
-        prep(NTU - 1, s, gval, true);
+        const int m = NTU - 1;
+        prep(RS + (m % 2) * SL, VS + (m % 3) * SL, VS + ((m + 1) % 3) * SL, AN + (m % 2) * SL,
+             AD + (m % 2) * SL, s, gval, true);
       }
     }
   }
   __syncthreads();
 
-  for (long long n = NTU - 1; n >= 0; --n) {
+  int t = T - 1, k = U - 1;  // n = t*U + k
+  for (int n = NTU - 1; n >= 0; --n) {
     // Tails of iteration m read V[m-1], V[m] and R[m-1]; prefetch what the tails
     // of the next iteration (n-1) need beyond that: V[n-2] and R[n-2].  Their
     // slots ((n+1)%3 and n%2) are not read in this iteration.
@@ -307,11 +313,15 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
     }
     cp_async_commit();
 
-    const int ci = (int)(n % 2);
-    const float* an_s = AN + ci * SL;
-    const float* ad_s = AD + ci * SL;
-    const float* vsn = VS + (int)(n % 3) * SL;
-    const int t = (int)(n / U), k = (int)(n % U);
+    const int c2 = n % 2, c2m = c2 ^ 1;          // slots of unfold n and n-1 (mod 2)
+    const int c3 = n % 3, c3m = (n + 2) % 3;     // slots of V[n] and V[n-1] (mod 3)
+    const float* an_s = AN + c2 * SL;
+    const float* ad_s = AD + c2 * SL;
+    const float* vsn = VS + c3 * SL;
+    const float* vsm = VS + c3m * SL;
+    const float* rsm = RS + c2m * SL;
+    float* an_m = AN + c2m * SL;
+    float* ad_m = AD + c2m * SL;
     for (int blk = 0; blk < nblk; ++blk) {
       float acc[1][G::NI];
 #pragma unroll
@@ -361,11 +371,15 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
             gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
           }
         }
-        if (!done) prep(n - 1, s, gval, k == 0);
+        if (!done) prep(rsm, vsm, vsn, an_m, ad_m, s, gval, k == 0);
       }
     }
     cp_async_wait_all();
     __syncthreads();
+    if (--k < 0) {
+      k = U - 1;
+      --t;
+    }
   }
 
   // partial gradients of this CTA
