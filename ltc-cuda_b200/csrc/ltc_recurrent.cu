@@ -93,6 +93,16 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
       cwp[r] += wp[r][j];
     }
   }
+  float2 sl2[RPT][4], nm2[RPT][4], wp2[RPT][4], we2[RPT][4];
+#pragma unroll
+  for (int r = 0; r < RPT; ++r)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      sl2[r][k] = make_float2(sl[r][2 * k], sl[r][2 * k + 1]);
+      nm2[r][k] = make_float2(nm[r][2 * k], nm[r][2 * k + 1]);
+      wp2[r][k] = make_float2(wp[r][2 * k], wp[r][2 * k + 1]);
+      we2[r][k] = make_float2(we[r][2 * k], we[r][2 * k + 1]);
+    }
 #endif
   // the one (column, sample-in-block) item this lane finishes
   const int own = LR::own_base(lane);
@@ -137,14 +147,17 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
           for (int r = 0; r < RPT; ++r) {
 #if LTC_FWD_TANH
             // act = 0.5 + 0.5*tanh(z/2): the constant halves are folded into
-            // cwe/cwp, the weights into the half-scale registers.
-            float sn_ = cwe[r], sd_ = cwp[r];
+            // cwe/cwp, the weights into the half-scale registers; synapses j and
+            // j+1 run as one packed f32x2 lane pair.
+            float2 sn2 = make_float2(cwe[r], 0.f), sd2 = make_float2(cwp[r], 0.f);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float th = tanh_approx(fmaf(sl[r][j], v8[j], nm[r][j]));
-              sn_ = fmaf(we[r][j], th, sn_);
-              sd_ = fmaf(wp[r][j], th, sd_);
+            for (int k = 0; k < 4; ++k) {
+              const float2 vv = make_float2(v8[2 * k], v8[2 * k + 1]);
+              const float2 th = tanh2(fma2(sl2[r][k], vv, nm2[r][k]));
+              sn2 = fma2(we2[r][k], th, sn2);
+              sd2 = fma2(wp2[r][k], th, sd2);
             }
+            const float sn_ = sn2.x + sn2.y, sd_ = sd2.x + sd2.y;
 #else
             float sn_ = 0.f, sd_ = 0.f;
 #pragma unroll
@@ -220,16 +233,22 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
   const int nblk = (nvalid + kSB - 1) / kSB;
   const int NTU = T * U;  // unfolds in the sequence
 
-  float sl[RPT][8], nm[RPT][8], wp[RPT][8], we[RPT][8];
-  float Gwe[RPT][8], Gwp[RPT][8], Gdz[RPT][8], Gdzv[RPT][8];
+  // synapses j = 2k, 2k+1 of a row are one packed f32x2 pair
+  float2 sl2[RPT][4], nm2[RPT][4], wp2[RPT][4], we2[RPT][4];
+  float2 Gwe[RPT][4], Gwp[RPT][4], Gdz[RPT][4], Gdzv[RPT][4];
 #pragma unroll
   for (int r = 0; r < RPT; ++r)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 pk = a.pack[(c + r * NG) * HP + G::sub(j, g)];
-      sl[r][j] = pk.x; nm[r][j] = pk.y; wp[r][j] = pk.z; we[r][j] = pk.w;
-      Gwe[r][j] = Gwp[r][j] = Gdz[r][j] = Gdzv[r][j] = 0.f;
+    for (int k = 0; k < 4; ++k) {
+      const float4 p0 = a.pack[(c + r * NG) * HP + G::sub(2 * k, g)];
+      const float4 p1 = a.pack[(c + r * NG) * HP + G::sub(2 * k + 1, g)];
+      sl2[r][k] = make_float2(p0.x, p1.x);
+      nm2[r][k] = make_float2(p0.y, p1.y);
+      wp2[r][k] = make_float2(p0.z, p1.z);
+      we2[r][k] = make_float2(p0.w, p1.w);
+      Gwe[r][k] = Gwp[r][k] = Gdz[r][k] = Gdzv[r][k] = make_float2(0.f, 0.f);
     }
+  const float2 half2 = make_float2(0.5f, 0.5f), nhalf2 = make_float2(-0.5f, -0.5f);
   // the one (row, sample-in-block) item this lane finishes
   const int own = LR::own_base(lane);
   const int orow = own / kSB, osmp = own % kSB;
@@ -333,24 +352,29 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
         const float4 a1 = *reinterpret_cast<const float4*>(ar + HP / 2);
         const float4 d0 = *reinterpret_cast<const float4*>(dr);
         const float4 d1 = *reinterpret_cast<const float4*>(dr + HP / 2);
-        const float an8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float ad8[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        const float2 an2[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                               make_float2(a1.z, a1.w)};
+        const float2 ad2[4] = {make_float2(d0.x, d0.y), make_float2(d0.z, d0.w), make_float2(d1.x, d1.y),
+                               make_float2(d1.z, d1.w)};
 #pragma unroll
         for (int r = 0; r < RPT; ++r) {
           const float vp = vsn[s * LDV + c + r * NG];
-          float dv = 0.f;
+          const float2 vp2 = make_float2(vp, vp);
+          float2 dv = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float act = gate_tanh(sl[r][j], nm[r][j], vp);
-            const float sp = fmaf(-act, act, act);
-            const float dz = fmaf(an8[j], we[r][j], ad8[j] * wp[r][j]) * sp;
-            Gwe[r][j] = fmaf(an8[j], act, Gwe[r][j]);
-            Gwp[r][j] = fmaf(ad8[j], act, Gwp[r][j]);
-            Gdz[r][j] += dz;
-            Gdzv[r][j] = fmaf(dz, vp, Gdzv[r][j]);
-            dv = fmaf(dz, sl[r][j], dv);
+          for (int k = 0; k < 4; ++k) {
+            // act = 0.5 + 0.5 tanh(z/2), 1 - act, act(1-act), then the adjoint terms
+            const float2 th = tanh2(fma2(sl2[r][k], vp2, nm2[r][k]));
+            const float2 act = fma2(half2, th, half2);
+            const float2 sp = mul2(act, fma2(nhalf2, th, half2));
+            const float2 dz = mul2(fma2(an2[k], we2[r][k], mul2(ad2[k], wp2[r][k])), sp);
+            Gwe[r][k] = fma2(an2[k], act, Gwe[r][k]);
+            Gwp[r][k] = fma2(ad2[k], act, Gwp[r][k]);
+            Gdz[r][k] = add2(Gdz[r][k], dz);
+            Gdzv[r][k] = fma2(dz, vp2, Gdzv[r][k]);
+            dv = fma2(dz, sl2[r][k], dv);
           }
-          acc[0][r * kSB + i] = dv;
+          acc[0][r * kSB + i] = dv.x + dv.y;
         }
       }
       LR::template run<1>(acc, lane);
@@ -389,10 +413,12 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int idx = (c + r * NG) * HP + G::sub(j, g);
-      part[idx] = Gwe[r][j];
-      part[HP * HP + idx] = Gwp[r][j];
-      part[2 * HP * HP + idx] = Gdz[r][j];
-      part[3 * HP * HP + idx] = Gdzv[r][j];
+      const int k = j / 2;
+      const bool hi = j & 1;
+      part[idx] = hi ? Gwe[r][k].y : Gwe[r][k].x;
+      part[HP * HP + idx] = hi ? Gwp[r][k].y : Gwp[r][k].x;
+      part[2 * HP * HP + idx] = hi ? Gdz[r][k].y : Gdz[r][k].x;
+      part[3 * HP * HP + idx] = hi ? Gdzv[r][k].y : Gdzv[r][k].x;
     }
   // per-neuron sums: each lane holds the partial of its own row; fixed-order sum
   // over the lanes of the group through shared memory.
