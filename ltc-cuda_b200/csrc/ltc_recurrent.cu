@@ -27,9 +27,20 @@ namespace {
 
 constexpr int kSB = 4;  // samples per register block
 
-template <int HP>
+// Neurons per thread and resident CTAs per SM of each kernel at HP = 64 (tuned on B200).
+#ifndef LTC_FWD_RPT
+#define LTC_FWD_RPT 1
+#endif
+#ifndef LTC_FWD_CTAS
+#define LTC_FWD_CTAS 1
+#endif
+#ifndef LTC_BWD_RPT
+#define LTC_BWD_RPT 2
+#endif
+
+template <int HP, int RPT_>
 struct Geometry {
-  static constexpr int RPT = HP >= 64 ? 2 : 1;  // neurons (rows / columns) per thread
+  static constexpr int RPT = RPT_;              // neurons (rows / columns) per thread
   static constexpr int TPC = HP / 8;            // lanes sharing a neuron group
   static constexpr int NG = HP / RPT;           // neuron groups
   static constexpr int NT = NG * TPC;           // threads
@@ -47,8 +58,15 @@ __device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
 }
 
 template <int HP>
-__global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a) {
-  using G = Geometry<HP>;
+constexpr int fwd_rpt() { return HP >= 64 ? LTC_FWD_RPT : 1; }
+template <int HP>
+constexpr int fwd_ctas() { return HP >= 64 ? LTC_FWD_CTAS : 1; }
+template <int HP>
+constexpr int bwd_rpt() { return HP >= 64 ? LTC_BWD_RPT : 1; }
+
+template <int HP>
+__global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>()) rec_fwd_fast(RecFwdArgs a) {
+  using G = Geometry<HP, fwd_rpt<HP>()>;
   constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV, RPT = G::RPT, NG = G::NG;
   using LR = LaneReduce<TPC, G::NI>;
   extern __shared__ __align__(16) float smem[];
@@ -209,8 +227,8 @@ __global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_fwd_fast(RecFwdArgs a
 //  DIR[s][p]     = direct term g*cm*r of the unfold being processed
 //  GSN/GSD[s][p] = running sums of a_n / a_d over the unfolds of the current step
 template <int HP>
-__global__ void __launch_bounds__(Geometry<HP>::NT, 1) rec_bwd_fast(RecBwdArgs a) {
-  using G = Geometry<HP>;
+__global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fast(RecBwdArgs a) {
+  using G = Geometry<HP, bwd_rpt<HP>()>;
   constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV, RPT = G::RPT, NG = G::NG;
   using LR = LaneReduce<TPC, G::NI>;
   extern __shared__ __align__(16) float smem[];
@@ -446,7 +464,7 @@ cudaError_t launch_fast_fwd(const RecFwdArgs& a, const RecPlan& pl, cudaStream_t
   cudaError_t e = cudaFuncSetAttribute(rec_fwd_fast<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)pl.smem_fwd);
   if (e != cudaSuccess) return e;
-  rec_fwd_fast<HP><<<pl.grid_fwd, Geometry<HP>::NT, pl.smem_fwd, st>>>(a);
+  rec_fwd_fast<HP><<<pl.grid_fwd, Geometry<HP, fwd_rpt<HP>()>::NT, pl.smem_fwd, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -455,7 +473,7 @@ cudaError_t launch_fast_bwd(const RecBwdArgs& a, const RecPlan& pl, cudaStream_t
   cudaError_t e = cudaFuncSetAttribute(rec_bwd_fast<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)pl.smem_bwd);
   if (e != cudaSuccess) return e;
-  rec_bwd_fast<HP><<<pl.grid_bwd, Geometry<HP>::NT, pl.smem_bwd, st>>>(a);
+  rec_bwd_fast<HP><<<pl.grid_bwd, Geometry<HP, bwd_rpt<HP>()>::NT, pl.smem_bwd, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -477,14 +495,21 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   const int HP = p.HP;
   const int LDV = HP + 4;
   const int blocks = (B + kSB - 1) / kSB;
-  // one CTA per SM when possible, each owning an equal share of sample blocks
-  int per = (blocks + num_sms - 1) / num_sms;
-  const int max_per = 64 / kSB;  // shared-memory bound for the backward kernel
-  if (per > max_per) per = max_per;
-  if (per < 1) per = 1;
-  p.ns_fwd = p.ns_bwd = per * kSB;
-  p.grid_fwd = p.grid_bwd = (B + p.ns_fwd - 1) / p.ns_fwd;
-  p.threads_fwd = p.threads_bwd = HP == 32 ? 128 : 256;
+  // each kernel: an equal share of sample blocks per resident CTA
+  auto share = [&](int ctas_per_sm) {
+    int per = (blocks + num_sms * ctas_per_sm - 1) / (num_sms * ctas_per_sm);
+    const int max_per = 64 / kSB;  // shared-memory bound
+    if (per > max_per) per = max_per;
+    if (per < 1) per = 1;
+    return per * kSB;
+  };
+  const bool h64 = HP >= 64;
+  p.ns_fwd = share(h64 ? LTC_FWD_CTAS : 1);
+  p.ns_bwd = share(1);
+  p.grid_fwd = (B + p.ns_fwd - 1) / p.ns_fwd;
+  p.grid_bwd = (B + p.ns_bwd - 1) / p.ns_bwd;
+  p.threads_fwd = HP * HP / 8 / (h64 ? LTC_FWD_RPT : 1);
+  p.threads_bwd = HP * HP / 8 / (h64 ? LTC_BWD_RPT : 1);
   p.slots_bwd = p.grid_bwd;
   p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
   p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 3 * HP * (HP / 8)) * sizeof(float);
