@@ -149,6 +149,6 @@ cudaError_t launch_finish(const FinishArgs& a, int num_sms, cudaStream_t st);
 void set_last_error(const char* msg);
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
-inline int pad_neurons(int H) { return H <= 32 ? 32 : (H <= 64 ? 64 : round_up(H, 32)); }
+inline int pad_neurons(int H) { return H <= 32 ? 32 : (H <= 64 ? 64 : (H <= 128 ? 128 : round_up(H, 32))); }
 
 }  // namespace ltc

@@ -18,8 +18,12 @@
 // free.  Per block of kSB samples, RPT*kSB partial sums are reduced across the
 // TPC lanes by a transposed (recursive-halving) reduction after which every lane
 // owns one (neuron, sample) item and runs its per-neuron "tail".
+#include <cooperative_groups.h>
+
 #include "ltc_common.cuh"
 #include "ltc_internal.h"
+
+namespace cg = cooperative_groups;
 
 namespace ltc {
 
@@ -38,11 +42,12 @@ constexpr int kSB = 4;  // samples per register block
 #define LTC_BWD_RPT 2
 #endif
 
-template <int HP, int RPT_>
+template <int HP, int RPT_, int CL>
 struct Geometry {
   static constexpr int RPT = RPT_;              // neurons (rows / columns) per thread
   static constexpr int TPC = HP / 8;            // lanes sharing a neuron group
-  static constexpr int NG = HP / RPT;           // neuron groups
+  static constexpr int NEUR = HP / CL;          // neurons owned by one CTA of the cluster
+  static constexpr int NG = NEUR / RPT;         // neuron groups
   static constexpr int NT = NG * TPC;           // threads
   static constexpr int NI = RPT * kSB;          // reduced items per block
   static constexpr int LDV = HP + 4;            // padded row stride of per-sample vectors
@@ -57,6 +62,33 @@ __device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
   return j < kMufuRcp ? gate(sl, nm, v) : gate_newton(sl, nm, v);
 }
 
+// Cluster helpers: with CL > 1 the CTAs of a cluster share one sample group and
+// each owns HP/CL neurons; per-neuron results are stored into every CTA's shared
+// memory (DSMEM) and the unfold barrier is the hardware cluster barrier.
+template <int CL>
+__device__ __forceinline__ void group_sync() {
+  if constexpr (CL > 1) cg::this_cluster().sync();
+  else __syncthreads();
+}
+template <int CL>
+__device__ __forceinline__ int group_rank() {
+  if constexpr (CL > 1) return (int)cg::this_cluster().block_rank();
+  else return 0;
+}
+template <int CL>
+__device__ __forceinline__ void store_all(float* local, float v) {
+  if constexpr (CL > 1) {
+    cg::cluster_group cl = cg::this_cluster();
+#pragma unroll
+    for (int r = 0; r < CL; ++r) *cl.map_shared_rank(local, r) = v;
+  } else {
+    *local = v;
+  }
+}
+
+template <int HP>
+constexpr int cluster_of() { return HP > 64 ? 4 : 1; }
+
 template <int HP>
 constexpr int fwd_rpt() { return HP >= 64 ? LTC_FWD_RPT : 1; }
 template <int HP>
@@ -65,8 +97,10 @@ template <int HP>
 constexpr int bwd_rpt() { return HP >= 64 ? LTC_BWD_RPT : 1; }
 
 template <int HP>
-__global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>()) rec_fwd_fast(RecFwdArgs a) {
-  using G = Geometry<HP, fwd_rpt<HP>()>;
+__global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>::NT, fwd_ctas<HP>())
+    rec_fwd_fast(RecFwdArgs a) {
+  constexpr int CL = cluster_of<HP>();
+  using G = Geometry<HP, fwd_rpt<HP>(), CL>;
   constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV, RPT = G::RPT, NG = G::NG;
   using LR = LaneReduce<TPC, G::NI>;
   extern __shared__ __align__(16) float smem[];
@@ -76,9 +110,10 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>(
   float* sdb = snb + ns * LDV;       // [ns][LDV]
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int c = tid / TPC, g = tid % TPC;
+  const int nb = group_rank<CL>() * G::NEUR;  // first neuron of this CTA
+  const int c = nb + tid / TPC, g = tid % TPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
-  const int b0 = blockIdx.x * ns;
+  const int b0 = (blockIdx.x / CL) * ns;
   const int nvalid = min(ns, B - b0);
   const int nblk = (nvalid + kSB - 1) / kSB;
 
@@ -139,6 +174,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>(
       vbuf[s * LDV + h] = a.h0[(long long)(b0 + s) * H + h];
     }
   }
+  group_sync<CL>();  // every CTA of the group initialised before any remote store
   int cur = 0;
   for (int t = 0; t < T; ++t) {
     __syncthreads();
@@ -198,7 +234,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>(
         const float rr = rcp_approx((cmgl + wd) + a.eps);
         const float vnew = num * rr;
         if (qvalid && writer && s < nvalid) {
-          vn[s * LDV + q] = vnew;
+          store_all<CL>(vn + s * LDV + q, vnew);
           const long long bs = b0 + s;
           if (a.V) {
             a.V[(n * B + bs) * H + q] = v;
@@ -207,13 +243,14 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>(
           if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
         }
       }
-      __syncthreads();
+      group_sync<CL>();
       cur ^= 1;
     }
   }
   const float* vc = vbuf + cur * ns * LDV;
-  for (int i = tid; i < nvalid * H; i += NT) {
-    const int s = i / H, h = i % H;
+  for (int i = tid; i < nvalid * G::NEUR; i += NT) {
+    const int s = i / G::NEUR, h = nb + i % G::NEUR;
+    if (h >= H) continue;
     const long long bs = b0 + s;
     a.hT[bs * H + h] = vc[s * LDV + h];
     if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[s * LDV + h];
@@ -227,8 +264,10 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>()>::NT, fwd_ctas<HP>(
 //  DIR[s][p]     = direct term g*cm*r of the unfold being processed
 //  GSN/GSD[s][p] = running sums of a_n / a_d over the unfolds of the current step
 template <int HP>
-__global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fast(RecBwdArgs a) {
-  using G = Geometry<HP, bwd_rpt<HP>()>;
+__global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>::NT, 1)
+    rec_bwd_fast(RecBwdArgs a) {
+  constexpr int CL = cluster_of<HP>();
+  using G = Geometry<HP, bwd_rpt<HP>(), CL>;
   constexpr int TPC = G::TPC, NT = G::NT, LDV = G::LDV, RPT = G::RPT, NG = G::NG;
   using LR = LaneReduce<TPC, G::NI>;
   extern __shared__ __align__(16) float smem[];
@@ -244,9 +283,11 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
   float* red = GSD + SL;
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int c = tid / TPC, g = tid % TPC;
+  const int nb = group_rank<CL>() * G::NEUR;  // first row of this CTA
+  const int c = nb + tid / TPC, g = tid % TPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
-  const int b0 = blockIdx.x * ns;
+  const int grp = blockIdx.x / CL;
+  const int b0 = grp * ns;
   const int nvalid = min(ns, B - b0);
   const int nblk = (nvalid + kSB - 1) / kSB;
   const int NTU = T * U;  // unfolds in the sequence
@@ -300,7 +341,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
   }
   cp_async_commit();
   cp_async_wait_all();
-  __syncthreads();
+  group_sync<CL>();  // every CTA of the group initialised before any remote store
 
   // Per-neuron prep of unfold m for (sample s, neuron p) given g = dL/dv_{m+1}[p]:
   // rs/vin/vout/an/ad point at the slabs of R[m], V[m], V[m+1] and the adjoint
@@ -319,8 +360,8 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
     GSN[idx] = first_of_step ? an : GSN[idx] + an;
     GSD[idx] = first_of_step ? ad : GSD[idx] + ad;
     DIR[idx] = an * cm;
-    an_d[idx] = an;
-    ad_d[idx] = ad;
+    store_all<CL>(an_d + idx, an);
+    store_all<CL>(ad_d + idx, ad);
   };
 
   // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate
@@ -337,7 +378,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
       }
     }
   }
-  __syncthreads();
+  group_sync<CL>();
 
   int t = T - 1, k = U - 1;  // n = t*U + k
   for (int n = NTU - 1; n >= 0; --n) {
@@ -417,7 +458,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
       }
     }
     cp_async_wait_all();
-    __syncthreads();
+    group_sync<CL>();
     if (--k < 0) {
       k = U - 1;
       --t;
@@ -425,7 +466,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
   }
 
   // partial gradients of this CTA
-  float* part = a.part + (long long)blockIdx.x * 4 * HP * HP;
+  float* part = a.part + (long long)grp * 4 * HP * HP;  // rows of the CTAs of a group are disjoint
 #pragma unroll
   for (int r = 0; r < RPT; ++r)
 #pragma unroll
@@ -448,33 +489,53 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>()>::NT, 1) rec_bwd_fa
     red[(2 * HP + p) * TPC + g] = gvl;
   }
   __syncthreads();
-  if (tid < HP) {
-    float* pn = a.partn + (long long)blockIdx.x * 3 * HP;
+  if (tid < G::NEUR) {
+    const int row = nb + tid;
+    float* pn = a.partn + (long long)grp * 3 * HP;
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
       float sum = 0.f;
-      for (int l = 0; l < TPC; ++l) sum += red[(k * HP + tid) * TPC + l];
-      pn[k * HP + tid] = sum;
+      for (int l = 0; l < TPC; ++l) sum += red[(k * HP + row) * TPC + l];
+      pn[k * HP + row] = sum;
     }
+  }
+}
+
+template <int CL, typename Args>
+cudaError_t launch_grouped(void (*kernel)(Args), const Args& a, int grid, int threads, size_t smem,
+                           cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if constexpr (CL == 1) {
+    kernel<<<grid, threads, smem, st>>>(a);
+    return cudaGetLastError();
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
   }
 }
 
 template <int HP>
 cudaError_t launch_fast_fwd(const RecFwdArgs& a, const RecPlan& pl, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(rec_fwd_fast<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)pl.smem_fwd);
-  if (e != cudaSuccess) return e;
-  rec_fwd_fast<HP><<<pl.grid_fwd, Geometry<HP, fwd_rpt<HP>()>::NT, pl.smem_fwd, st>>>(a);
-  return cudaGetLastError();
+  return launch_grouped<cluster_of<HP>()>(rec_fwd_fast<HP>, a, pl.grid_fwd,
+                                          Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>::NT, pl.smem_fwd, st);
 }
 
 template <int HP>
 cudaError_t launch_fast_bwd(const RecBwdArgs& a, const RecPlan& pl, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(rec_bwd_fast<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)pl.smem_bwd);
-  if (e != cudaSuccess) return e;
-  rec_bwd_fast<HP><<<pl.grid_bwd, Geometry<HP, bwd_rpt<HP>()>::NT, pl.smem_bwd, st>>>(a);
-  return cudaGetLastError();
+  return launch_grouped<cluster_of<HP>()>(rec_bwd_fast<HP>, a, pl.grid_bwd,
+                                          Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>::NT, pl.smem_bwd, st);
 }
 
 }  // namespace
@@ -487,30 +548,34 @@ void plan_wide(RecPlan& p, int B, int H, int num_sms);
 RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   RecPlan p{};
   p.HP = pad_neurons(H);
-  p.wide = force_wide || H > 64;
+  p.wide = force_wide || H > 128;
   if (p.wide) {
     plan_wide(p, B, H, num_sms);
     return p;
   }
-  const int HP = p.HP;
+  const int HP = p.HP;  // 32, 64 or 128
   const int LDV = HP + 4;
+  const int CL = HP > 64 ? 4 : 1;  // cluster_of<HP>()
+  const int groups = num_sms / CL;
   const int blocks = (B + kSB - 1) / kSB;
-  // each kernel: an equal share of sample blocks per resident CTA
-  auto share = [&](int ctas_per_sm) {
-    int per = (blocks + num_sms * ctas_per_sm - 1) / (num_sms * ctas_per_sm);
-    const int max_per = 64 / kSB;  // shared-memory bound
+  // each kernel: an equal share of sample blocks per resident sample group
+  // shared-memory bound of the backward kernel (13 per-sample slabs + the reduction area)
+  const size_t smem_cap = 227 * 1024 - 1024;
+  const int max_per = (int)((smem_cap - 3 * HP * (HP / 8) * sizeof(float)) / (13 * LDV * sizeof(float) * kSB));
+  auto share = [&](int groups_per_pass) {
+    int per = (blocks + groups_per_pass - 1) / groups_per_pass;
     if (per > max_per) per = max_per;
     if (per < 1) per = 1;
     return per * kSB;
   };
   const bool h64 = HP >= 64;
-  p.ns_fwd = share(h64 ? LTC_FWD_CTAS : 1);
-  p.ns_bwd = share(1);
-  p.grid_fwd = (B + p.ns_fwd - 1) / p.ns_fwd;
-  p.grid_bwd = (B + p.ns_bwd - 1) / p.ns_bwd;
-  p.threads_fwd = HP * HP / 8 / (h64 ? LTC_FWD_RPT : 1);
-  p.threads_bwd = HP * HP / 8 / (h64 ? LTC_BWD_RPT : 1);
-  p.slots_bwd = p.grid_bwd;
+  p.ns_fwd = share(groups * (h64 ? LTC_FWD_CTAS : 1));
+  p.ns_bwd = share(groups);
+  p.grid_fwd = CL * ((B + p.ns_fwd - 1) / p.ns_fwd);
+  p.grid_bwd = CL * ((B + p.ns_bwd - 1) / p.ns_bwd);
+  p.threads_fwd = HP * HP / 8 / CL / (h64 ? LTC_FWD_RPT : 1);
+  p.threads_bwd = HP * HP / 8 / CL / (h64 ? LTC_BWD_RPT : 1);
+  p.slots_bwd = p.grid_bwd / CL;
   p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
   p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 3 * HP * (HP / 8)) * sizeof(float);
   return p;
@@ -518,12 +583,20 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
 
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
   if (p.wide) return launch_wide_fwd(a, p, st);
-  return p.HP == 32 ? launch_fast_fwd<32>(a, p, st) : launch_fast_fwd<64>(a, p, st);
+  switch (p.HP) {
+    case 32: return launch_fast_fwd<32>(a, p, st);
+    case 64: return launch_fast_fwd<64>(a, p, st);
+    default: return launch_fast_fwd<128>(a, p, st);
+  }
 }
 
 cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st) {
   if (p.wide) return launch_wide_bwd(a, p, st);
-  return p.HP == 32 ? launch_fast_bwd<32>(a, p, st) : launch_fast_bwd<64>(a, p, st);
+  switch (p.HP) {
+    case 32: return launch_fast_bwd<32>(a, p, st);
+    case 64: return launch_fast_bwd<64>(a, p, st);
+    default: return launch_fast_bwd<128>(a, p, st);
+  }
 }
 
 }  // namespace ltc
