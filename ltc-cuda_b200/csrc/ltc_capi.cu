@@ -155,7 +155,7 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
 
 struct FwdBuffers {
   float4 *pack, *spack, *nrn;
-  float *sn, *sd;
+  float *sn, *sd, *scratch;
 };
 size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
   Carver c(ws);
@@ -165,12 +165,13 @@ size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
   b->nrn = c.take<float4>(HP);
   b->sn = c.take<float>((size_t)L.rows * d->H);
   b->sd = c.take<float>((size_t)L.rows * d->H);
+  b->scratch = L.rp.scratch_fwd ? c.take<float>(L.rp.scratch_fwd) : nullptr;
   return c.off + 256;
 }
 
 struct BwdBuffers {
   float4 *pack, *packT, *spack, *nrn;
-  float *gsn, *gsd, *rpart, *rpartn, *spart, *dxpart;
+  float *gsn, *gsd, *rpart, *rpartn, *spart, *dxpart, *scratch;
 };
 size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   Carver c(ws);
@@ -185,6 +186,7 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->rpartn = c.take<float>((size_t)L.rp.slots_bwd * 3 * HP);
   b->spart = c.take<float>(L.sp.part_floats);
   b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
+  b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
   return c.off + 256;
 }
 
@@ -311,7 +313,7 @@ int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, co
     ra.R = c.take<float>(L.saved_floats_r);
   }
   ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
-  ra.ns = L.rp.ns_fwd; ra.eps = dims->epsilon;
+  ra.ns = L.rp.ns_fwd; ra.eps = dims->epsilon; ra.scratch = b.scratch;
   {
     TimedLaunch tl(LTC_KERNEL_RECURRENT_FWD, st);
     e = launch_recurrent_fwd(ra, L.rp, st);
@@ -361,7 +363,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   ra.gstate = grad_state; ra.gsn = b.gsn; ra.gsd = b.gsd; ra.gh0 = grads->state;
   ra.part = b.rpart; ra.partn = b.rpartn;
   ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
-  ra.ns = L.rp.ns_bwd;
+  ra.ns = L.rp.ns_bwd; ra.scratch = b.scratch;
   {
     TimedLaunch tl(LTC_KERNEL_RECURRENT_BWD, st);
     e = launch_recurrent_bwd(ra, L.rp, st);
@@ -378,7 +380,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   if (e != cudaSuccess) return cuda_fail(e, "sensory_bwd");
 
   FinishArgs fa{};
-  fa.rec_part = b.rpart; fa.rec_partn = b.rpartn; fa.rslots = L.rp.slots_bwd; fa.rec_transposed = L.rp.wide;
+  fa.rec_part = b.rpart; fa.rec_partn = b.rpartn; fa.rslots = L.rp.slots_bwd; fa.rec_transposed = L.rp.wide && !L.rp.streamed;
   fa.sens_part = b.spart; fa.nsplit = L.sp.nsplit; fa.dxpart = b.dxpart; fa.nqc = L.sp.nqc; fa.rows = L.rows;
   fa.mu = params->mu; fa.sigma = params->sigma; fa.smu = params->sensory_mu; fa.ssig = params->sensory_sigma;
   fa.serev = params->sensory_erev; fa.sw = params->sensory_w_pos;

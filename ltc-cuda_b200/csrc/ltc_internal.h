@@ -92,6 +92,7 @@ struct RecFwdArgs {
   int B, T, H, U, HP;
   int ns;               // samples per CTA
   float eps;
+  float* scratch;       // plan.scratch_fwd floats (streamed path)
 };
 struct RecBwdArgs {
   const float4* pack;   // [HP][HP] (fast path)
@@ -109,9 +110,12 @@ struct RecBwdArgs {
   float* partn;         // [slots][3][HP]
   int B, T, H, U, HP;
   int ns;
+  float* scratch;       // plan.scratch_bwd floats (streamed path)
 };
 struct RecPlan {
-  bool wide;       // generic (wide-H) kernels instead of the register-resident ones
+  bool wide;       // not the register-resident kernels (streamed or generic wide-H)
+  bool streamed;   // cluster-streamed kernels (128 < H <= 512)
+  size_t scratch_fwd, scratch_bwd;  // floats of path-specific global scratch
   int HP;          // padded neuron count
   int ns_fwd, grid_fwd, threads_fwd;
   size_t smem_fwd;

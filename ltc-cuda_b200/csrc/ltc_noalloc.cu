@@ -88,12 +88,14 @@ extern "C" int ltc_forward_noalloc(const LtcDims* dims, const LtcParams* params,
   const int HP = rp.HP;
   const long long rows = (long long)B * T;
   // scratch layout: pack [HP*HP] float4 | spack [D*HP] float4 | nrn [HP] float4 | sn [rows*H] | sd [rows*H]
+  //                 | recurrent-kernel scratch (the streamed path for H > 128)
   const size_t o_pack = 0;
   const size_t o_spack = align256(o_pack + (size_t)HP * HP * sizeof(float4));
   const size_t o_nrn = align256(o_spack + (size_t)D * HP * sizeof(float4));
   const size_t o_sn = align256(o_nrn + (size_t)HP * sizeof(float4));
   const size_t o_sd = align256(o_sn + (size_t)rows * H * sizeof(float));
-  const size_t need = o_sd + (size_t)rows * H * sizeof(float);
+  const size_t o_scr = align256(o_sd + (size_t)rows * H * sizeof(float));
+  const size_t need = o_scr + rp.scratch_fwd * sizeof(float);
   if (need > (size_t)LTC_NOALLOC_SCRATCH_BYTES) {
     char buf[256];
     snprintf(buf, sizeof(buf),
@@ -128,6 +130,7 @@ extern "C" int ltc_forward_noalloc(const LtcDims* dims, const LtcParams* params,
       ra.pack = pa.pack; ra.nrn = pa.nrn; ra.sn = sa.sn; ra.sd = sa.sd; ra.h0 = h0;
       ra.out = outputs; ra.hT = h_final; ra.V = nullptr; ra.R = nullptr;
       ra.B = B; ra.T = T; ra.H = H; ra.U = U; ra.HP = HP; ra.ns = rp.ns_fwd; ra.eps = dims->epsilon;
+      ra.scratch = rp.scratch_fwd ? reinterpret_cast<float*>(base + o_scr) : nullptr;
       e = launch_recurrent_fwd(ra, rp, st);
     }
   }

@@ -544,13 +544,21 @@ cudaError_t launch_fast_bwd(const RecBwdArgs& a, const RecPlan& pl, cudaStream_t
 cudaError_t launch_wide_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
 cudaError_t launch_wide_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
 void plan_wide(RecPlan& p, int B, int H, int num_sms);
+// cluster-streamed kernels (ltc_recurrent_stream.cu)
+cudaError_t launch_stream_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
+cudaError_t launch_stream_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
+void plan_stream(RecPlan& p, int B, int H, int num_sms);
 
 RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   RecPlan p{};
   p.HP = pad_neurons(H);
-  p.wide = force_wide || H > 128;
-  if (p.wide) {
+  if (force_wide) {
+    p.wide = true;
     plan_wide(p, B, H, num_sms);
+    return p;
+  }
+  if (H > 128) {
+    plan_stream(p, B, H, num_sms);
     return p;
   }
   const int HP = p.HP;  // 32, 64 or 128
@@ -582,6 +590,7 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
 }
 
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  if (p.streamed) return launch_stream_fwd(a, p, st);
   if (p.wide) return launch_wide_fwd(a, p, st);
   switch (p.HP) {
     case 32: return launch_fast_fwd<32>(a, p, st);
@@ -591,6 +600,7 @@ cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStre
 }
 
 cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  if (p.streamed) return launch_stream_bwd(a, p, st);
   if (p.wide) return launch_wide_bwd(a, p, st);
   switch (p.HP) {
     case 32: return launch_fast_bwd<32>(a, p, st);

@@ -1,0 +1,459 @@
+// Cluster-streamed recurrent kernels for 128 < H <= 512 (padded to HP = 256 or 512).
+//
+// The dense H x H synapse set (4 gate-pack floats + 4 gradient sums per synapse:
+// 8 MB at H = 512) fits in no CTA or cluster, so each 8-CTA cluster owns one
+// group of `ns` samples and each CTA owns NEUR = HP/8 neurons:
+//   forward : CTA = columns [nb, nb+NEUR); per unfold it streams the pack rows
+//             (chunks of PC presynaptic rows x its columns) and the matching
+//             slice of every sample's state through double-buffered shared
+//             memory (cp.async), thread = (column, sample subgroup).
+//   backward: CTA = rows [nb, nb+NEUR); per unfold it streams column chunks of
+//             its pack rows and of its gradient slab (4 sums per synapse, kept in
+//             L2: 4*NEUR*HP floats per CTA), thread = (row, 8 columns), and
+//             accumulates every synapse over all ns samples in registers before
+//             writing the chunk back -- one read-modify-write per synapse per
+//             unfold for the whole sample group.
+// Per-neuron vectors (state in the forward; a_n, a_d in the backward) are
+// exchanged through global memory (L2) and ordered by the hardware cluster
+// barrier (release/acquire at cluster scope), one barrier per unfold.
+#include <cooperative_groups.h>
+
+#include "ltc_common.cuh"
+#include "ltc_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace ltc {
+
+namespace {
+
+constexpr int kCL = 8;    // CTAs per cluster
+constexpr int kNT = 256;  // threads per CTA
+constexpr int kPC = 32;   // presynaptic rows per forward chunk
+constexpr int kSB = 4;    // samples per register block (backward)
+
+template <int NEUR>
+struct SGeom {
+  static constexpr int HP = NEUR * kCL;
+  static constexpr int SGF = kNT / NEUR;  // forward sample subgroups
+  static constexpr int QL = kNT / NEUR;   // backward lanes per row
+  static constexpr int QC = QL * 8;       // backward columns per chunk
+};
+
+__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
+
+// --------------------------------------------------------------------------- forward
+template <int NEUR, int NSPT>
+__global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
+  using G = SGeom<NEUR>;
+  constexpr int HP = G::HP, SGF = G::SGF, NC = HP / kPC;
+  extern __shared__ __align__(16) float smem[];
+  const int ns = SGF * NSPT;
+  float4* pks = reinterpret_cast<float4*>(smem);     // [2][kPC][NEUR]
+  float* vch = smem + 2 * 4 * kPC * NEUR;            // [2][ns][kPC]
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x;
+  const int nb = (int)cluster.block_rank() * NEUR;
+  const int ql = tid % NEUR, sg = tid / NEUR;
+  const int q = nb + ql;
+  const int H = a.H, B = a.B, T = a.T, U = a.U;
+  const int b0 = (blockIdx.x / kCL) * ns;
+  const int nvalid = min(ns, B - b0);
+  float* vstate = a.scratch;  // [2][B][HP]
+  const long long SB_ = (long long)B * HP;
+
+  // per-column constants: 0.5 * sum_p w (the act = 0.5 + 0.5 tanh split)
+  float ce = 0.f, cp = 0.f;
+  for (int p = 0; p < HP; ++p) {
+    const float4 w = a.pack[(long long)p * HP + q];
+    ce += w.w;
+    cp += w.z;
+  }
+  const float4 nq = a.nrn[q];
+  const float cm = nq.x, cmgl = nq.x + nq.y, glvl = nq.w;
+  const bool qvalid = q < H;
+
+  // both state buffers: the padded neurons must read as 0 in every unfold
+  for (int i = tid; i < nvalid * NEUR; i += kNT) {
+    const int s = i / NEUR, h = nb + i % NEUR;
+    const long long o = (long long)(b0 + s) * HP + h;
+    vstate[o] = (a.h0 && h < H) ? a.h0[(long long)(b0 + s) * H + h] : 0.f;
+    vstate[SB_ + o] = 0.f;
+  }
+  cluster.sync();
+
+  auto stage = [&](int c, int buf, const float* vcur) {
+    float4* dst = pks + buf * kPC * NEUR;
+    for (int i = tid; i < kPC * NEUR; i += kNT) {
+      const int pp = i / NEUR, cc = i % NEUR;
+      cp_async16(dst + i, a.pack + (long long)(c * kPC + pp) * HP + nb + cc);
+    }
+    float* vd = vch + buf * ns * kPC;
+    for (int i = tid; i < nvalid * (kPC / 4); i += kNT) {
+      const int s = i / (kPC / 4), k4 = i % (kPC / 4);
+      cp_async16(vd + s * kPC + 4 * k4, vcur + (long long)(b0 + s) * HP + c * kPC + 4 * k4);
+    }
+    cp_async_commit();
+  };
+
+  int cur = 0;
+  for (int t = 0; t < T; ++t) {
+    for (int u = 0; u < U; ++u) {
+      const long long n = (long long)t * U + u;
+      const float* vc = vstate + cur * SB_;
+      float* vn = vstate + (cur ^ 1) * SB_;
+      float an[NSPT], ad[NSPT];
+#pragma unroll
+      for (int i = 0; i < NSPT; ++i) an[i] = ad[i] = 0.f;
+      stage(0, 0, vc);
+      for (int c = 0; c < NC; ++c) {
+        cp_async_wait_all();
+        __syncthreads();
+        if (c + 1 < NC) stage(c + 1, (c + 1) & 1, vc);
+        const float4* pk = pks + (c & 1) * kPC * NEUR + ql;
+        const float* vr = vch + (c & 1) * ns * kPC + sg * kPC;
+#pragma unroll 4
+        for (int pp = 0; pp < kPC; ++pp) {
+          const float4 w = pk[pp * NEUR];
+#pragma unroll
+          for (int i = 0; i < NSPT; ++i) {
+            const float th = tanh_approx(fmaf(w.x, vr[i * SGF * kPC + pp], w.y));
+            an[i] = fmaf(w.w, th, an[i]);
+            ad[i] = fmaf(w.z, th, ad[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NSPT; ++i) {
+        const int s = sg + i * SGF;
+        if (s < nvalid && qvalid) {
+          const long long bs = b0 + s;
+          const long long row = bs * T + t;
+          const float v = vc[bs * HP + q];
+          const float num = (cm * v + glvl) + (0.5f * (ce + an[i]) + a.sn[row * H + q]);
+          const float r = rcp_approx((cmgl + (0.5f * (cp + ad[i]) + a.sd[row * H + q])) + a.eps);
+          const float vnew = num * r;
+          vn[bs * HP + q] = vnew;
+          if (a.V) {
+            a.V[(n * B + bs) * H + q] = v;
+            a.R[(n * B + bs) * H + q] = r;
+          }
+          if (u == U - 1) a.out[row * H + q] = vnew;
+        }
+      }
+      cluster.sync();  // release this unfold's states / acquire the peers'
+      cur ^= 1;
+    }
+  }
+  const float* vc = vstate + cur * SB_;
+  for (int i = tid; i < nvalid * NEUR; i += kNT) {
+    const int s = i / NEUR, h = nb + i % NEUR;
+    if (h >= H) continue;
+    const long long bs = b0 + s;
+    a.hT[bs * H + h] = vc[bs * HP + h];
+    if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[bs * HP + h];
+  }
+}
+
+// --------------------------------------------------------------------------- backward
+// scratch layout: AN, AD [2][B][HP] (by unfold parity), DIR, GSN, GSD [B][HP]
+template <int NEUR>
+__global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
+  using G = SGeom<NEUR>;
+  constexpr int HP = G::HP, QL = G::QL, QC = G::QC, NC = HP / QC;
+  using LR = LaneReduce<QL, kSB>;
+  extern __shared__ __align__(16) float smem[];
+  const int ns = a.ns;
+  float4* pks = reinterpret_cast<float4*>(smem);        // [2][NEUR][QC]
+  float* gch = smem + 2 * 4 * NEUR * QC;                // [2][4][NEUR][QC]
+  float* anc = gch + 2 * 4 * NEUR * QC;                 // [2][ns][QC]
+  float* adc = anc + 2 * ns * QC;                       // [2][ns][QC]
+  float* DV = adc + 2 * ns * QC;                        // [ns][NEUR]
+  float* VP = DV + ns * NEUR;                           // [ns][NEUR]
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nb = (int)cluster.block_rank() * NEUR;
+  const int rl = tid / QL, ql = tid % QL;
+  const int p = nb + rl;
+  const int H = a.H, B = a.B, T = a.T, U = a.U;
+  const int grp = blockIdx.x / kCL;
+  const int b0 = grp * ns;
+  const int nvalid = min(ns, B - b0);
+  const int NTU = T * U;
+  const long long SB_ = (long long)B * HP;
+  float* ANg = a.scratch;
+  float* ADg = ANg + 2 * SB_;
+  float* DIRg = ADg + 2 * SB_;
+  float* GSNg = DIRg + SB_;
+  float* GSDg = GSNg + SB_;
+  const long long hp2 = (long long)HP * HP;
+  float* slab = a.part + (long long)grp * 4 * hp2;  // rows of the CTAs of a cluster are disjoint
+  const float4 np_ = a.nrn[p];
+  const float cm = np_.x, gl = np_.y, vl = np_.z;
+  const bool pvalid = p < H;
+  float gcm = 0.f, ggl = 0.f, gvl = 0.f;
+
+  // adjoint rows of padded samples in the last register block must read as 0
+  const int nblk = (nvalid + kSB - 1) / kSB;
+  for (int i = tid; i < 2 * (nblk * kSB - nvalid) * QC; i += kNT) {
+    const int buf = i / ((nblk * kSB - nvalid) * QC), rem = i % ((nblk * kSB - nvalid) * QC);
+    const int s = nvalid + rem / QC, cc = rem % QC;
+    anc[(buf * ns + s) * QC + cc] = 0.f;
+    adc[(buf * ns + s) * QC + cc] = 0.f;
+  }
+  // zero this CTA's rows of the gradient slab
+  for (int i = tid; i < NEUR * HP; i += kNT) {
+    const long long o = (long long)(nb + i / HP) * HP + i % HP;
+    slab[o] = 0.f;
+    slab[hp2 + o] = 0.f;
+    slab[2 * hp2 + o] = 0.f;
+    slab[3 * hp2 + o] = 0.f;
+  }
+
+  // prep of unfold m for (sample s, own row p) given g = dL/dv_{m+1}[p]
+  auto prep = [&](int m, int s, float gval, bool first) {
+    const long long bs = b0 + s;
+    const float r = a.R[((long long)m * B + bs) * H + p];
+    const float vin = a.V[((long long)m * B + bs) * H + p];
+    const float vout = a.V[((long long)(m + 1) * B + bs) * H + p];
+    const float an = gval * r;
+    const float ad = -an * vout;
+    gcm = fmaf(an, vin - vout, gcm);
+    ggl = fmaf(an, vl - vout, ggl);
+    gvl = fmaf(an, gl, gvl);
+    const long long o = bs * HP + p;
+    GSNg[o] = first ? an : GSNg[o] + an;
+    GSDg[o] = first ? ad : GSDg[o] + ad;
+    DIRg[o] = an * cm;
+    ANg[(m & 1) * SB_ + o] = an;
+    ADg[(m & 1) * SB_ + o] = ad;
+  };
+
+  // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate; padded rows write zeros
+  for (int s = ql; s < ns; s += QL) {
+    const long long bs = b0 + s;
+    if (s >= nvalid) continue;
+    if (pvalid) {
+      float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
+      if (a.gstate) gval += a.gstate[bs * H + p];
+      prep(NTU - 1, s, gval, true);
+    } else {
+      for (int par = 0; par < 2; ++par) {
+        ANg[par * SB_ + bs * HP + p] = 0.f;
+        ADg[par * SB_ + bs * HP + p] = 0.f;
+      }
+    }
+  }
+  cluster.sync();
+
+  auto stage = [&](int n, int c, int buf) {
+    float4* pd = pks + buf * NEUR * QC;
+    for (int i = tid; i < NEUR * QC; i += kNT) {
+      const int r = i / QC, cc = i % QC;
+      cp_async16(pd + i, a.pack + (long long)(nb + r) * HP + c * QC + cc);
+    }
+    float* gd = gch + buf * 4 * NEUR * QC;
+    for (int i = tid; i < 4 * NEUR * (QC / 4); i += kNT) {
+      const int k = i / (NEUR * (QC / 4)), rem = i % (NEUR * (QC / 4));
+      const int r = rem / (QC / 4), c4 = rem % (QC / 4);
+      cp_async16(gd + (k * NEUR + r) * QC + 4 * c4, slab + k * hp2 + (long long)(nb + r) * HP + c * QC + 4 * c4);
+    }
+    const float* asrc = ANg + (n & 1) * SB_;
+    const float* dsrc = ADg + (n & 1) * SB_;
+    float* ad_ = anc + buf * ns * QC;
+    float* dd_ = adc + buf * ns * QC;
+    for (int i = tid; i < nvalid * (QC / 4); i += kNT) {
+      const int s = i / (QC / 4), c4 = i % (QC / 4);
+      const long long o = (long long)(b0 + s) * HP + c * QC + 4 * c4;
+      cp_async16(ad_ + s * QC + 4 * c4, asrc + o);
+      cp_async16(dd_ + s * QC + 4 * c4, dsrc + o);
+    }
+    cp_async_commit();
+  };
+
+  const int own = LR::own_base(lane);
+  const bool writer = LR::writer(lane);
+  const float2 half2 = make_float2(0.5f, 0.5f), nhalf2 = make_float2(-0.5f, -0.5f);
+  int t = T - 1, k = U - 1;
+  for (int n = NTU - 1; n >= 0; --n) {
+    for (int i = tid; i < ns * NEUR; i += kNT) {
+      const int s = i / NEUR, r = i % NEUR;
+      DV[i] = 0.f;
+      VP[i] = (s < nvalid && nb + r < H) ? a.V[((long long)n * B + b0 + s) * H + nb + r] : 0.f;
+    }
+    stage(n, 0, 0);
+    for (int c = 0; c < NC; ++c) {
+      cp_async_wait_all();
+      __syncthreads();
+      if (c + 1 < NC) stage(n, c + 1, (c + 1) & 1);
+      const int buf = c & 1;
+      float2 sl2[4], nm2[4], wp2[4], we2[4], G0[4], G1[4], G2[4], G3[4];
+      const float4* pk = pks + buf * NEUR * QC + rl * QC + ql * 8;
+      const float* gsrc = gch + buf * 4 * NEUR * QC + rl * QC + ql * 8;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 p0 = pk[2 * kk], p1 = pk[2 * kk + 1];
+        sl2[kk] = make_float2(p0.x, p1.x);
+        nm2[kk] = make_float2(p0.y, p1.y);
+        wp2[kk] = make_float2(p0.z, p1.z);
+        we2[kk] = make_float2(p0.w, p1.w);
+        G0[kk] = *reinterpret_cast<const float2*>(gsrc + 2 * kk);
+        G1[kk] = *reinterpret_cast<const float2*>(gsrc + NEUR * QC + 2 * kk);
+        G2[kk] = *reinterpret_cast<const float2*>(gsrc + 2 * NEUR * QC + 2 * kk);
+        G3[kk] = *reinterpret_cast<const float2*>(gsrc + 3 * NEUR * QC + 2 * kk);
+      }
+      const float* ans = anc + buf * ns * QC + ql * 8;
+      const float* ads = adc + buf * ns * QC + ql * 8;
+      for (int blk = 0; blk < nblk; ++blk) {
+        float acc[1][kSB];
+#pragma unroll
+        for (int i = 0; i < kSB; ++i) {
+          const int s = blk * kSB + i;
+          const float4 a0 = *reinterpret_cast<const float4*>(ans + s * QC);
+          const float4 a1 = *reinterpret_cast<const float4*>(ans + s * QC + 4);
+          const float4 d0 = *reinterpret_cast<const float4*>(ads + s * QC);
+          const float4 d1 = *reinterpret_cast<const float4*>(ads + s * QC + 4);
+          const float2 an2[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                                 make_float2(a1.z, a1.w)};
+          const float2 ad2[4] = {make_float2(d0.x, d0.y), make_float2(d0.z, d0.w), make_float2(d1.x, d1.y),
+                                 make_float2(d1.z, d1.w)};
+          const float vp = VP[s * NEUR + rl];
+          const float2 vp2 = make_float2(vp, vp);
+          float2 dv = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const float2 th = tanh2(fma2(sl2[kk], vp2, nm2[kk]));
+            const float2 act = fma2(half2, th, half2);
+            const float2 sp = mul2(act, fma2(nhalf2, th, half2));
+            const float2 dz = mul2(fma2(an2[kk], we2[kk], mul2(ad2[kk], wp2[kk])), sp);
+            G0[kk] = fma2(an2[kk], act, G0[kk]);
+            G1[kk] = fma2(ad2[kk], act, G1[kk]);
+            G2[kk] = add2(G2[kk], dz);
+            G3[kk] = fma2(dz, vp2, G3[kk]);
+            dv = fma2(dz, sl2[kk], dv);
+          }
+          acc[0][i] = dv.x + dv.y;
+        }
+        LR::template run<1>(acc, lane);
+        const int s = blk * kSB + own;
+        if (writer && s < nvalid) DV[s * NEUR + rl] += acc[0][0];
+      }
+      // write the chunk's gradient sums back to the slab (L2)
+      float* gdst = slab + (long long)p * HP + c * QC + ql * 8;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        *reinterpret_cast<float2*>(gdst + 2 * kk) = G0[kk];
+        *reinterpret_cast<float2*>(gdst + hp2 + 2 * kk) = G1[kk];
+        *reinterpret_cast<float2*>(gdst + 2 * hp2 + 2 * kk) = G2[kk];
+        *reinterpret_cast<float2*>(gdst + 3 * hp2 + 2 * kk) = G3[kk];
+      }
+    }
+    __syncthreads();
+    // per-neuron tails of the own rows
+    for (int s = ql; s < nvalid; s += QL) {
+      if (!pvalid) continue;
+      const long long bs = b0 + s;
+      const long long o = bs * HP + p;
+      float gval = fmaf(2.0f, DV[s * NEUR + rl], ldcg(DIRg + o));  // sl holds sigma/2
+      if (k == 0) {
+        const long long row = bs * T + t;
+        a.gsn[row * H + p] = ldcg(GSNg + o);
+        a.gsd[row * H + p] = ldcg(GSDg + o);
+        if (t == 0) {
+          a.gh0[bs * H + p] = gval;
+          continue;
+        }
+        gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
+      }
+      prep(n - 1, s, gval, k == 0);
+    }
+    cluster.sync();  // release a_n/a_d of unfold n-1 / acquire the peers'
+    if (--k < 0) {
+      k = U - 1;
+      --t;
+    }
+  }
+  // per-neuron partial sums: reduce over the QL lanes of the row (fixed order)
+#pragma unroll
+  for (int stride = QL / 2; stride >= 1; stride >>= 1) {
+    gcm += __shfl_xor_sync(0xffffffffu, gcm, stride);
+    ggl += __shfl_xor_sync(0xffffffffu, ggl, stride);
+    gvl += __shfl_xor_sync(0xffffffffu, gvl, stride);
+  }
+  if (ql == 0) {
+    float* pn = a.partn + (long long)grp * 3 * HP;
+    pn[p] = gcm;
+    pn[HP + p] = ggl;
+    pn[2 * HP + p] = gvl;
+  }
+}
+
+template <typename Args>
+cudaError_t launch_cluster8(void (*kernel)(Args), const Args& a, int grid, size_t smem, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kNT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
+template <int NEUR>
+cudaError_t fwd_dispatch(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  switch (p.ns_fwd / SGeom<NEUR>::SGF) {
+    case 1: return launch_cluster8(rec_fwd_stream<NEUR, 1>, a, p.grid_fwd, p.smem_fwd, st);
+    case 2: return launch_cluster8(rec_fwd_stream<NEUR, 2>, a, p.grid_fwd, p.smem_fwd, st);
+    case 4: return launch_cluster8(rec_fwd_stream<NEUR, 4>, a, p.grid_fwd, p.smem_fwd, st);
+    case 8: return launch_cluster8(rec_fwd_stream<NEUR, 8>, a, p.grid_fwd, p.smem_fwd, st);
+    default: return launch_cluster8(rec_fwd_stream<NEUR, 16>, a, p.grid_fwd, p.smem_fwd, st);
+  }
+}
+
+}  // namespace
+
+void plan_stream(RecPlan& p, int B, int H, int num_sms) {
+  const int HP = H <= 256 ? 256 : 512;
+  const int NEUR = HP / kCL;
+  const int SGF = kNT / NEUR, QC = (kNT / NEUR) * 8;
+  p.HP = HP;
+  p.wide = true;
+  p.streamed = true;
+  const int groups = num_sms / kCL;
+  const int max_nspt = NEUR == 64 ? 16 : 8;  // 64 samples per group at most
+  int want = (B + groups - 1) / groups;
+  int nspt = 1;
+  while (nspt < max_nspt && nspt * SGF < want) nspt *= 2;
+  const int ns = nspt * SGF;  // a multiple of kSB
+  p.ns_fwd = p.ns_bwd = ns;
+  const int ngroups = (B + ns - 1) / ns;
+  p.grid_fwd = p.grid_bwd = ngroups * kCL;
+  p.threads_fwd = p.threads_bwd = kNT;
+  p.slots_bwd = ngroups;
+  p.smem_fwd = (size_t)2 * kPC * NEUR * 16 + (size_t)2 * ns * kPC * 4;
+  p.smem_bwd = (size_t)2 * NEUR * QC * 16 + (size_t)2 * 4 * NEUR * QC * 4 + (size_t)4 * ns * QC * 4 +
+               (size_t)2 * ns * NEUR * 4;
+  p.scratch_fwd = (size_t)2 * B * HP;
+  p.scratch_bwd = (size_t)7 * B * HP;
+}
+
+cudaError_t launch_stream_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  return p.HP == 256 ? fwd_dispatch<32>(a, p, st) : fwd_dispatch<64>(a, p, st);
+}
+
+cudaError_t launch_stream_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  return p.HP == 256 ? launch_cluster8(rec_bwd_stream<32>, a, p.grid_bwd, p.smem_bwd, st)
+                     : launch_cluster8(rec_bwd_stream<64>, a, p.grid_bwd, p.smem_bwd, st);
+}
+
+}  // namespace ltc
