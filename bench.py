@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=None,
                     help="override the configuration's global batch (profiling captures of smaller cases)")
+    ap.add_argument("--seq", type=int, default=None, help="override the sequence length T (profiling captures)")
     return ap.parse_args()
 
 
@@ -194,6 +195,9 @@ def main():
     if args.batch is not None:
         import dataclasses
         cfg = dataclasses.replace(cfg, B=args.batch)
+    if args.seq is not None:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, T=args.seq)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -103,9 +103,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
       const long long n = (long long)t * U + u;
       const float* vc = vstate + cur * SB_;
       float* vn = vstate + (cur ^ 1) * SB_;
-      float an[NSPT], ad[NSPT];
+      float2 an[NSPT], ad[NSPT];  // (even, odd) presynaptic rows, summed at the end
 #pragma unroll
-      for (int i = 0; i < NSPT; ++i) an[i] = ad[i] = 0.f;
+      for (int i = 0; i < NSPT; ++i) an[i] = ad[i] = make_float2(0.f, 0.f);
       stage(0, 0, vc);
       for (int c = 0; c < NC; ++c) {
         cp_async_wait_all();
@@ -113,14 +113,21 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
         if (c + 1 < NC) stage(c + 1, (c + 1) & 1, vc);
         const float4* pk = pks + (c & 1) * kPC * NEUR + ql;
         const float* vr = vch + (c & 1) * ns * kPC + sg * kPC;
-#pragma unroll 4
-        for (int pp = 0; pp < kPC; ++pp) {
-          const float4 w = pk[pp * NEUR];
+#pragma unroll 2
+        for (int pp = 0; pp < kPC; pp += 4) {
+          const float4 w0 = pk[pp * NEUR], w1 = pk[(pp + 1) * NEUR];
+          const float4 w2 = pk[(pp + 2) * NEUR], w3 = pk[(pp + 3) * NEUR];
+          const float2 sx01 = make_float2(w0.x, w1.x), sy01 = make_float2(w0.y, w1.y);
+          const float2 sz01 = make_float2(w0.z, w1.z), sw01 = make_float2(w0.w, w1.w);
+          const float2 sx23 = make_float2(w2.x, w3.x), sy23 = make_float2(w2.y, w3.y);
+          const float2 sz23 = make_float2(w2.z, w3.z), sw23 = make_float2(w2.w, w3.w);
 #pragma unroll
           for (int i = 0; i < NSPT; ++i) {
-            const float th = tanh_approx(fmaf(w.x, vr[i * SGF * kPC + pp], w.y));
-            an[i] = fmaf(w.w, th, an[i]);
-            ad[i] = fmaf(w.z, th, ad[i]);
+            const float4 v4 = *reinterpret_cast<const float4*>(vr + i * SGF * kPC + pp);
+            const float2 t01 = tanh2(fma2(sx01, make_float2(v4.x, v4.y), sy01));
+            const float2 t23 = tanh2(fma2(sx23, make_float2(v4.z, v4.w), sy23));
+            an[i] = fma2(sw23, t23, fma2(sw01, t01, an[i]));
+            ad[i] = fma2(sz23, t23, fma2(sz01, t01, ad[i]));
           }
         }
       }
@@ -131,8 +138,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
           const long long bs = b0 + s;
           const long long row = bs * T + t;
           const float v = vc[bs * HP + q];
-          const float num = (cm * v + glvl) + (0.5f * (ce + an[i]) + a.sn[row * H + q]);
-          const float r = rcp_approx((cmgl + (0.5f * (cp + ad[i]) + a.sd[row * H + q])) + a.eps);
+          const float num = (cm * v + glvl) + (0.5f * (ce + (an[i].x + an[i].y)) + a.sn[row * H + q]);
+          const float r = rcp_approx((cmgl + (0.5f * (cp + (ad[i].x + ad[i].y)) + a.sd[row * H + q])) + a.eps);
           const float vnew = num * r;
           vn[bs * HP + q] = vnew;
           if (a.V) {
@@ -165,8 +172,10 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   using LR = LaneReduce<QL, kSB>;
   extern __shared__ __align__(16) float smem[];
   const int ns = a.ns;
-  float4* pks = reinterpret_cast<float4*>(smem);        // [2][NEUR][QC]
-  float* gch = smem + 2 * 4 * NEUR * QC;                // [2][4][NEUR][QC]
+  // pack / gradient chunks are staged thread-major ([slot][thread]) so that each
+  // thread's 8 synapses are read without bank conflicts
+  float4* pks = reinterpret_cast<float4*>(smem);        // [2][8][kNT]   (pack of synapse j)
+  float* gch = smem + 2 * 4 * NEUR * QC;                // [2][4][2][kNT] float4 (sums k, j-half)
   float* anc = gch + 2 * 4 * NEUR * QC;                 // [2][ns][QC]
   float* adc = anc + 2 * ns * QC;                       // [2][ns][QC]
   float* DV = adc + 2 * ns * QC;                        // [ns][NEUR]
@@ -249,16 +258,17 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   cluster.sync();
 
   auto stage = [&](int n, int c, int buf) {
-    float4* pd = pks + buf * NEUR * QC;
-    for (int i = tid; i < NEUR * QC; i += kNT) {
-      const int r = i / QC, cc = i % QC;
-      cp_async16(pd + i, a.pack + (long long)(nb + r) * HP + c * QC + cc);
+    // thread th = (row th/QL, lane th%QL) owns columns c*QC + (th%QL)*8 + j
+    float4* pd = pks + buf * 8 * kNT;
+    for (int i = tid; i < 8 * kNT; i += kNT) {
+      const int j = i / kNT, th = i % kNT;
+      cp_async16(pd + i, a.pack + (long long)(nb + th / QL) * HP + c * QC + (th % QL) * 8 + j);
     }
-    float* gd = gch + buf * 4 * NEUR * QC;
-    for (int i = tid; i < 4 * NEUR * (QC / 4); i += kNT) {
-      const int k = i / (NEUR * (QC / 4)), rem = i % (NEUR * (QC / 4));
-      const int r = rem / (QC / 4), c4 = rem % (QC / 4);
-      cp_async16(gd + (k * NEUR + r) * QC + 4 * c4, slab + k * hp2 + (long long)(nb + r) * HP + c * QC + 4 * c4);
+    float4* gd = reinterpret_cast<float4*>(gch) + buf * 8 * kNT;
+    for (int i = tid; i < 8 * kNT; i += kNT) {
+      const int kh = i / kNT, th = i % kNT;  // kh = k*2 + half
+      const int k = kh / 2, half = kh % 2;
+      cp_async16(gd + i, slab + k * hp2 + (long long)(nb + th / QL) * HP + c * QC + (th % QL) * 8 + 4 * half);
     }
     const float* asrc = ANg + (n & 1) * SB_;
     const float* dsrc = ADg + (n & 1) * SB_;
@@ -290,36 +300,43 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       if (c + 1 < NC) stage(n, c + 1, (c + 1) & 1);
       const int buf = c & 1;
       float2 sl2[4], nm2[4], wp2[4], we2[4], G0[4], G1[4], G2[4], G3[4];
-      const float4* pk = pks + buf * NEUR * QC + rl * QC + ql * 8;
-      const float* gsrc = gch + buf * 4 * NEUR * QC + rl * QC + ql * 8;
+      const float4* pk = pks + buf * 8 * kNT + tid;
+      const float4* gs = reinterpret_cast<const float4*>(gch) + buf * 8 * kNT + tid;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const float4 p0 = pk[2 * kk], p1 = pk[2 * kk + 1];
+        const float4 p0 = pk[(2 * kk) * kNT], p1 = pk[(2 * kk + 1) * kNT];
         sl2[kk] = make_float2(p0.x, p1.x);
         nm2[kk] = make_float2(p0.y, p1.y);
         wp2[kk] = make_float2(p0.z, p1.z);
         we2[kk] = make_float2(p0.w, p1.w);
-        G0[kk] = *reinterpret_cast<const float2*>(gsrc + 2 * kk);
-        G1[kk] = *reinterpret_cast<const float2*>(gsrc + NEUR * QC + 2 * kk);
-        G2[kk] = *reinterpret_cast<const float2*>(gsrc + 2 * NEUR * QC + 2 * kk);
-        G3[kk] = *reinterpret_cast<const float2*>(gsrc + 3 * NEUR * QC + 2 * kk);
+      }
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const float4 g0 = gs[(0 + h2) * kNT], g1 = gs[(2 + h2) * kNT];
+        const float4 g2 = gs[(4 + h2) * kNT], g3 = gs[(6 + h2) * kNT];
+        G0[2 * h2] = make_float2(g0.x, g0.y); G0[2 * h2 + 1] = make_float2(g0.z, g0.w);
+        G1[2 * h2] = make_float2(g1.x, g1.y); G1[2 * h2 + 1] = make_float2(g1.z, g1.w);
+        G2[2 * h2] = make_float2(g2.x, g2.y); G2[2 * h2 + 1] = make_float2(g2.z, g2.w);
+        G3[2 * h2] = make_float2(g3.x, g3.y); G3[2 * h2 + 1] = make_float2(g3.z, g3.w);
       }
       const float* ans = anc + buf * ns * QC + ql * 8;
       const float* ads = adc + buf * ns * QC + ql * 8;
-      for (int blk = 0; blk < nblk; ++blk) {
+      const float* vps = VP + rl;
+      float* dvs = DV + own * NEUR + rl;
+      for (int blk = 0; blk < nblk; ++blk, ans += kSB * QC, ads += kSB * QC, vps += kSB * NEUR,
+               dvs += kSB * NEUR) {
         float acc[1][kSB];
 #pragma unroll
         for (int i = 0; i < kSB; ++i) {
-          const int s = blk * kSB + i;
-          const float4 a0 = *reinterpret_cast<const float4*>(ans + s * QC);
-          const float4 a1 = *reinterpret_cast<const float4*>(ans + s * QC + 4);
-          const float4 d0 = *reinterpret_cast<const float4*>(ads + s * QC);
-          const float4 d1 = *reinterpret_cast<const float4*>(ads + s * QC + 4);
+          const float4 a0 = *reinterpret_cast<const float4*>(ans + i * QC);
+          const float4 a1 = *reinterpret_cast<const float4*>(ans + i * QC + 4);
+          const float4 d0 = *reinterpret_cast<const float4*>(ads + i * QC);
+          const float4 d1 = *reinterpret_cast<const float4*>(ads + i * QC + 4);
           const float2 an2[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
                                  make_float2(a1.z, a1.w)};
           const float2 ad2[4] = {make_float2(d0.x, d0.y), make_float2(d0.z, d0.w), make_float2(d1.x, d1.y),
                                  make_float2(d1.z, d1.w)};
-          const float vp = VP[s * NEUR + rl];
+          const float vp = vps[i * NEUR];
           const float2 vp2 = make_float2(vp, vp);
           float2 dv = make_float2(0.f, 0.f);
 #pragma unroll
@@ -337,8 +354,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
           acc[0][i] = dv.x + dv.y;
         }
         LR::template run<1>(acc, lane);
-        const int s = blk * kSB + own;
-        if (writer && s < nvalid) DV[s * NEUR + rl] += acc[0][0];
+        if (writer && blk * kSB + own < nvalid) *dvs += acc[0][0];
       }
       // write the chunk's gradient sums back to the slab (L2)
       float* gdst = slab + (long long)p * HP + c * QC + ql * 8;
