@@ -102,6 +102,21 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
                  const float* grad_outputs, const int64_t go_strides[3], const float* grad_state,
                  const LtcGrads* grads, void* workspace, size_t workspace_bytes, ltc_stream_t stream);
 
+/* Module preamble, fused (replaces the PyTorch ops of ltc.py:259 and ltc.py:266):
+ *   y = (LayerNorm(x) * ln_w + ln_b) * in_w + in_b     over the last dim D <= 1024,
+ * biased variance, eps as nn.LayerNorm.  x, y: (rows, D); stats: (rows, 2) =
+ * (mean, 1/sqrt(var+eps)) kept for the backward.  The backward writes dx and the
+ * four (D) parameter gradients (deterministic, fixed-order reductions) and needs
+ * a workspace of ltc_preamble_workspace_bytes(rows, D) bytes. */
+int ltc_preamble_forward(int64_t rows, int32_t D, float eps, const float* x, const float* ln_w,
+                         const float* ln_b, const float* in_w, const float* in_b, float* y, float* stats,
+                         ltc_stream_t stream);
+size_t ltc_preamble_workspace_bytes(int64_t rows, int32_t D);
+int ltc_preamble_backward(int64_t rows, int32_t D, const float* x, const float* dy, const float* ln_w,
+                          const float* ln_b, const float* in_w, const float* stats, float* dx, float* g_ln_w,
+                          float* g_ln_b, float* g_in_w, float* g_in_b, void* workspace, size_t workspace_bytes,
+                          ltc_stream_t stream);
+
 /* Size of the fixed device scratch array behind ltc_forward_noalloc (16 MiB per GPU). */
 #define LTC_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
@@ -120,7 +135,8 @@ int ltc_forward_noalloc(const LtcDims* dims, const LtcParams* params, const floa
                         float* outputs, float* h_final, ltc_stream_t stream);
 
 /* Kernel identifiers of the launches each call issues (forward: PACK_FWD,
- * SENSORY_FWD, RECURRENT_FWD; backward: PACK_BWD, RECURRENT_BWD, SENSORY_BWD, FINISH). */
+ * SENSORY_FWD, RECURRENT_FWD; backward: PACK_BWD, RECURRENT_BWD, SENSORY_BWD, FINISH; the fused
+ * module preamble: PREAMBLE_FWD, PREAMBLE_BWD). */
 enum {
   LTC_KERNEL_PACK_FWD = 0,
   LTC_KERNEL_SENSORY_FWD = 1,
@@ -129,7 +145,9 @@ enum {
   LTC_KERNEL_RECURRENT_BWD = 4,
   LTC_KERNEL_SENSORY_BWD = 5,
   LTC_KERNEL_FINISH = 6,
-  LTC_NUM_KERNELS = 7
+  LTC_KERNEL_PREAMBLE_FWD = 7,
+  LTC_KERNEL_PREAMBLE_BWD = 8,
+  LTC_NUM_KERNELS = 9
 };
 
 /* Per-launch device timing, process-wide (no counterpart in the

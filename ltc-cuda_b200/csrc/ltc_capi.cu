@@ -248,6 +248,66 @@ int ltc_timing_collect(double* total_ms, int32_t* launches, int n) {
   return 0;
 }
 
+size_t ltc_preamble_workspace_bytes(int64_t rows, int32_t D) {
+  int err = 0;
+  const DeviceInfo di = device_info(&err);
+  if (err || rows < 1 || D < 1) return 0;
+  return (size_t)preamble_blocks(rows, di.sms) * 4 * D * sizeof(float);
+}
+
+int ltc_preamble_forward(int64_t rows, int32_t D, float eps, const float* x, const float* ln_w,
+                         const float* ln_b, const float* in_w, const float* in_b, float* y, float* stats,
+                         ltc_stream_t stream) {
+  if (rows < 1 || D < 1 || D > 1024) return fail("ltc_preamble_forward: need rows >= 1 and 1 <= D <= 1024");
+  if (!x || !ln_w || !ln_b || !in_w || !in_b || !y || !stats) return fail("ltc_preamble_forward: NULL pointer");
+  int err = 0;
+  const DeviceInfo di = device_info(&err);
+  if (err) return 1;
+  PreambleArgs a{};
+  a.x = x; a.ln_w = ln_w; a.ln_b = ln_b; a.in_w = in_w; a.in_b = in_b; a.y = y; a.stats = stats;
+  a.rows = rows; a.D = D; a.eps = eps;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  {
+    TimedLaunch tl(LTC_KERNEL_PREAMBLE_FWD, st);
+    e = launch_preamble_fwd(a, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "preamble_fwd");
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_preamble_backward(int64_t rows, int32_t D, const float* x, const float* dy, const float* ln_w,
+                          const float* ln_b, const float* in_w, const float* stats, float* dx, float* g_ln_w,
+                          float* g_ln_b, float* g_in_w, float* g_in_b, void* workspace, size_t workspace_bytes,
+                          ltc_stream_t stream) {
+  if (rows < 1 || D < 1 || D > 1024) return fail("ltc_preamble_backward: need rows >= 1 and 1 <= D <= 1024");
+  if (!x || !dy || !ln_w || !ln_b || !in_w || !stats || !dx || !g_ln_w || !g_ln_b || !g_in_w || !g_in_b ||
+      !workspace)
+    return fail("ltc_preamble_backward: NULL pointer");
+  int err = 0;
+  const DeviceInfo di = device_info(&err);
+  if (err) return 1;
+  const size_t need = (size_t)preamble_blocks(rows, di.sms) * 4 * D * sizeof(float);
+  if (workspace_bytes < need)
+    return fail("ltc_preamble_backward: workspace of %zu bytes is smaller than the %zu bytes required",
+                workspace_bytes, need);
+  PreambleArgs a{};
+  a.x = x; a.dy = dy; a.ln_w = ln_w; a.ln_b = ln_b; a.in_w = in_w; a.stats = const_cast<float*>(stats); a.dx = dx;
+  a.part = static_cast<float*>(workspace);
+  a.g_in_w = g_in_w; a.g_in_b = g_in_b; a.g_ln_w = g_ln_w; a.g_ln_b = g_ln_b;
+  a.rows = rows; a.D = D;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  {
+    TimedLaunch tl(LTC_KERNEL_PREAMBLE_BWD, st);
+    e = launch_preamble_bwd(a, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "preamble_bwd");
+  g_last_error.clear();
+  return 0;
+}
+
 int64_t ltc_launch_count(void) {
   std::lock_guard<std::mutex> lk(g_tm_mu);
   return g_tm.launches;

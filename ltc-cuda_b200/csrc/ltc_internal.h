@@ -149,6 +149,24 @@ struct FinishArgs {
 };
 cudaError_t launch_finish(const FinishArgs& a, int num_sms, cudaStream_t st);
 
+// ---- module preamble: LayerNorm + input affine ---------------------------
+struct PreambleArgs {
+  const float* x;       // (rows, D) raw input
+  const float* dy;      // (rows, D) gradient of the preamble output (backward)
+  const float* ln_w; const float* ln_b; const float* in_w; const float* in_b;  // (D)
+  float* y;             // (rows, D) output (forward)
+  float* dx;            // (rows, D) input gradient (backward)
+  float* stats;         // (rows, 2) mean, rstd
+  float* part;          // [blocks][4][D] column-gradient partials (backward)
+  float* g_in_w; float* g_in_b; float* g_ln_w; float* g_ln_b;  // (D)
+  long long rows;
+  int D;
+  float eps;
+};
+int preamble_blocks(long long rows, int num_sms);
+cudaError_t launch_preamble_fwd(const PreambleArgs& a, int num_sms, cudaStream_t st);
+cudaError_t launch_preamble_bwd(const PreambleArgs& a, int num_sms, cudaStream_t st);
+
 // Error reporting shared by every extern "C" entry point (ltc_last_error()).
 void set_last_error(const char* msg);
 

@@ -74,6 +74,12 @@ EXPORTS = {
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64),
                                     ctypes.c_void_p, ctypes.POINTER(LtcGrads), ctypes.c_void_p,
                                     ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_preamble_forward": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_float] + [ctypes.c_void_p] * 8),
+    "ltc_preamble_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32]),
+    "ltc_preamble_backward": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32] + [ctypes.c_void_p] * 12
+                              + [ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams)]
+                            + [ctypes.c_void_p] * 5),
     "ltc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
     "ltc_timing_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32),
                                           ctypes.c_int]),
@@ -155,7 +161,7 @@ def set_force_wide(on: bool) -> None:
 
 
 KERNEL_NAMES = ("pack_fwd", "sensory_fwd", "recurrent_fwd", "pack_bwd", "recurrent_bwd", "sensory_bwd",
-                "finish")
+                "finish", "preamble_fwd", "preamble_bwd")
 
 
 def timing_enable(on: bool) -> None:
@@ -324,3 +330,55 @@ def ltc_cuda_forward(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory
     return LTCCudaForward.apply(x_seq, state, w_pos, w_erev, mu, sigma, sensory_mu, sensory_sigma,
                                 sensory_erev, sensory_w_pos, cm_t, gleak_pos, vleak, ode_unfolds, epsilon,
                                 needs_grad)
+
+
+# ---------------------------------------------------------------------------
+# Fused module preamble: LayerNorm + input affine map (ltc.py:259, ltc.py:266)
+# ---------------------------------------------------------------------------
+PREAMBLE_MAX_D = 1024
+
+
+class LtcPreamble(torch.autograd.Function):
+    """y = (LayerNorm(x; ln_w, ln_b, eps) * in_w + in_b) in one sm_100a kernel per direction."""
+
+    @staticmethod
+    def forward(ctx, x, ln_w, ln_b, in_w, in_b, eps: float):
+        lib = _require_kernels()
+        dev = x.device
+        xc = _as_f32(x, dev, "x")
+        D = xc.shape[-1]
+        rows = xc.numel() // D
+        params = [_as_f32(t, dev, n) for t, n in ((ln_w, "ln_w"), (ln_b, "ln_b"), (in_w, "in_w"), (in_b, "in_b"))]
+        y = torch.empty_like(xc)
+        stats = torch.empty(rows, 2, device=dev, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            st = torch.cuda.current_stream(dev).cuda_stream
+            _check(lib.ltc_preamble_forward(rows, D, float(eps), xc.data_ptr(), *[t.data_ptr() for t in params],
+                                            y.data_ptr(), stats.data_ptr(), st), "ltc_preamble_forward")
+        ctx.save_for_backward(xc, params[0], params[1], params[2], stats)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        lib = _require_kernels()
+        xc, ln_w, ln_b, in_w, stats = ctx.saved_tensors
+        dev = xc.device
+        D = xc.shape[-1]
+        rows = xc.numel() // D
+        dyc = dy.to(torch.float32).contiguous()
+        dx = torch.empty_like(xc)
+        grads = [torch.empty(D, device=dev, dtype=torch.float32) for _ in range(4)]  # ln_w, ln_b, in_w, in_b
+        with torch.cuda.device(dev):
+            nbytes = lib.ltc_preamble_workspace_bytes(rows, D)
+            ws = torch.empty(max(1, nbytes), dtype=torch.uint8, device=dev)
+            st = torch.cuda.current_stream(dev).cuda_stream
+            _check(lib.ltc_preamble_backward(rows, D, xc.data_ptr(), dyc.data_ptr(), ln_w.data_ptr(),
+                                             ln_b.data_ptr(), in_w.data_ptr(), stats.data_ptr(), dx.data_ptr(),
+                                             *[g.data_ptr() for g in grads], ws.data_ptr(), nbytes, st),
+                   "ltc_preamble_backward")
+        return dx, grads[0], grads[1], grads[2], grads[3], None
+
+
+def ltc_preamble(x, ln_w, ln_b, in_w, in_b, eps: float):
+    """Fused LayerNorm + affine map over the last dimension (D <= 1024)."""
+    return LtcPreamble.apply(x, ln_w, ln_b, in_w, in_b, eps)

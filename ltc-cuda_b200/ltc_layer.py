@@ -107,10 +107,16 @@ class TrueLiquidTimeConstant(nn.Module):
         state = torch.zeros(B, self.hidden_dim, device=x_seq.device, dtype=x_seq.dtype)
         if h0 is not None:
             state = h0[0]
-        x = self.input_norm(x_seq)
+        if (_solver is ltc_cuda.ltc_cuda_forward and x_seq.is_cuda and x_seq.dtype == torch.float32
+                and D <= ltc_cuda.PREAMBLE_MAX_D):
+            # LayerNorm + affine map fused in one kernel each way (same arithmetic as below)
+            x = ltc_cuda.ltc_preamble(x_seq, self.input_norm.weight, self.input_norm.bias, self.input_w,
+                                      self.input_b, self.input_norm.eps)
+        else:
+            x = self.input_norm(x_seq)
+            x = x * self.input_w + self.input_b
         if state.dtype != x.dtype:
             state = state.to(x.dtype)
-        x = x * self.input_w + self.input_b
         w_pos, w_erev, cm_t, gleak_pos, sensory_w_pos = self._transforms()
         if _solver is ltc_cuda.ltc_cuda_forward and not (x.is_cuda and x.dtype == torch.float32):
             raise RuntimeError(f"TrueLiquidTimeConstant: the sm_100a solver needs fp32 CUDA input "
