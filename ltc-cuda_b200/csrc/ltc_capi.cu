@@ -183,7 +183,7 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->gsn = c.take<float>((size_t)L.rows * d->H);
   b->gsd = c.take<float>((size_t)L.rows * d->H);
   b->rpart = c.take<float>((size_t)L.rp.slots_bwd * 4 * HP * HP);
-  b->rpartn = c.take<float>((size_t)L.rp.slots_bwd * 3 * HP);
+  b->rpartn = c.take<float>((size_t)L.rp.slots_bwd * 5 * HP);
   b->spart = c.take<float>(L.sp.part_floats);
   b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
   b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
@@ -441,6 +441,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
 
   FinishArgs fa{};
   fa.rec_part = b.rpart; fa.rec_partn = b.rpartn; fa.rslots = L.rp.slots_bwd; fa.rec_transposed = L.rp.wide && !L.rp.streamed;
+  fa.rec_tanh_space = L.rp.tanh_space;
   fa.sens_part = b.spart; fa.nsplit = L.sp.nsplit; fa.dxpart = b.dxpart; fa.nqc = L.sp.nqc; fa.rows = L.rows;
   fa.mu = params->mu; fa.sigma = params->sigma; fa.smu = params->sensory_mu; fa.ssig = params->sensory_sigma;
   fa.serev = params->sensory_erev; fa.sw = params->sensory_w_pos;

@@ -107,7 +107,7 @@ struct RecBwdArgs {
   float* gsd;           // (B*T, H)
   float* gh0;           // (B,H)
   float* part;          // [slots][4][HP*HP]  synapse partials, layout [p][q] (fast) / [q][p] (wide)
-  float* partn;         // [slots][3][HP]
+  float* partn;         // [slots][3 or 5][HP] (see RecPlan::tanh_space)
   int B, T, H, U, HP;
   int ns;
   float* scratch;       // plan.scratch_bwd floats (streamed path)
@@ -115,6 +115,7 @@ struct RecBwdArgs {
 struct RecPlan {
   bool wide;       // not the register-resident kernels (streamed or generic wide-H)
   bool streamed;   // cluster-streamed kernels (128 < H <= 512)
+  bool tanh_space; // synapse partials hold sum a'*tanh (a' = -a/4); partn has 5 rows (+ sum a_n, sum a_d)
   size_t scratch_fwd, scratch_bwd;  // floats of path-specific global scratch
   int HP;          // padded neuron count
   int ns_fwd, grid_fwd, threads_fwd;
@@ -129,9 +130,10 @@ cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStre
 // ---- deterministic reductions and final gradient transforms --------------
 struct FinishArgs {
   const float* rec_part;   // [rslots][4][HP*HP]
-  const float* rec_partn;  // [rslots][3][HP]
+  const float* rec_partn;  // [rslots][3 or 5][HP]
   int rslots;
   bool rec_transposed;     // partial layout [q][p]
+  bool rec_tanh_space;     // S0/S1 are sums of a'*tanh (a' = -a/4), partn rows 3/4 = sums of a_n/a_d
   const float* sens_part;  // [nsplit][4][D*HP]
   int nsplit;
   const float* dxpart;     // [nqc][rows*D] or null

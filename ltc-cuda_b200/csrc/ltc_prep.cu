@@ -85,15 +85,26 @@ __global__ void finish_kernel(FinishArgs a) {
         s2 += base[2 * hp2];
         s3 += base[3 * hp2];
       }
+      if (a.rec_tanh_space) {
+        // sum a*act = sum a/2 + 2 * sum a'*tanh  with a' = -a/4, tanh = tanh(-z/2)
+        float san = 0.f, sad = 0.f;
+        for (int c = 0; c < a.rslots; ++c) {
+          san += a.rec_partn[((long long)c * 5 + 3) * a.HP + q];
+          sad += a.rec_partn[((long long)c * 5 + 4) * a.HP + q];
+        }
+        s0 = fmaf(0.5f, san, 2.0f * s0);
+        s1 = fmaf(0.5f, sad, 2.0f * s1);
+      }
       a.g_w_erev[i] = s0;
       a.g_w_pos[i] = s1;
       a.g_mu[i] = -a.sigma[i] * s2;
       a.g_sigma[i] = s3 - a.mu[i] * s2;
     } else if (i < nrec + nneu) {
       const int q = (int)(i - nrec);
+      const int kn = a.rec_tanh_space ? 5 : 3;
       float s0 = 0.f, s1 = 0.f, s2 = 0.f;
       for (int c = 0; c < a.rslots; ++c) {
-        const float* base = a.rec_partn + (long long)c * 3 * a.HP + q;
+        const float* base = a.rec_partn + (long long)c * kn * a.HP + q;
         s0 += base[0];
         s1 += base[a.HP];
         s2 += base[2 * a.HP];

@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   float* RS = VS + 3 * SL;   // [2]
   float* DIR = RS + 2 * SL;
   float* GSN = DIR + SL;
-  float* GSD = GSN + SL;     // 13 slabs, then [3][HP][TPC] for the final per-neuron sums
+  float* GSD = GSN + SL;     // 13 slabs, then [5][HP][TPC] for the final per-neuron sums
   float* red = GSD + SL;
 
   const int tid = threadIdx.x, lane = tid & 31;
@@ -301,13 +301,14 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     for (int k = 0; k < 4; ++k) {
       const float4 p0 = a.pack[(c + r * NG) * HP + G::sub(2 * k, g)];
       const float4 p1 = a.pack[(c + r * NG) * HP + G::sub(2 * k + 1, g)];
-      sl2[r][k] = make_float2(p0.x, p1.x);
-      nm2[r][k] = make_float2(p0.y, p1.y);
+      // negated half-scale constants: the gate argument is -z/2, so tanh gives -t
+      sl2[r][k] = make_float2(-p0.x, -p1.x);
+      nm2[r][k] = make_float2(-p0.y, -p1.y);
       wp2[r][k] = make_float2(p0.z, p1.z);
       we2[r][k] = make_float2(p0.w, p1.w);
       Gwe[r][k] = Gwp[r][k] = Gdz[r][k] = Gdzv[r][k] = make_float2(0.f, 0.f);
     }
-  const float2 half2 = make_float2(0.5f, 0.5f), nhalf2 = make_float2(-0.5f, -0.5f);
+  const float2 m1 = make_float2(-1.f, -1.f);
   // the one (row, sample-in-block) item this lane finishes
   const int own = LR::own_base(lane);
   const int orow = own / kSB, osmp = own % kSB;
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   const float cm = np_.x, gl = np_.y, vl = np_.z;
   const bool pvalid = p < H;
   const bool writer = LR::writer(lane);
-  float gcm = 0.f, ggl = 0.f, gvl = 0.f;
+  float gcm = 0.f, ggl = 0.f, gvl = 0.f, san = 0.f, sad = 0.f;
 
   for (int i = tid; i < 13 * SL; i += NT) smem[i] = 0.f;
   __syncthreads();
@@ -357,11 +358,14 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     gcm = fmaf(an, vin - vout, gcm);
     ggl = fmaf(an, vl - vout, ggl);
     gvl = fmaf(an, gl, gvl);
+    san += an;
+    sad += ad;
     GSN[idx] = first_of_step ? an : GSN[idx] + an;
     GSD[idx] = first_of_step ? ad : GSD[idx] + ad;
     DIR[idx] = an * cm;
-    store_all<CL>(an_d + idx, an);
-    store_all<CL>(ad_d + idx, ad);
+    // the synapse pass works in tanh space: it reads a' = -a/4 (see the pass)
+    store_all<CL>(an_d + idx, -0.25f * an);
+    store_all<CL>(ad_d + idx, -0.25f * ad);
   };
 
   // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate
@@ -422,13 +426,13 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
           float2 dv = make_float2(0.f, 0.f);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            // act = 0.5 + 0.5 tanh(z/2), 1 - act, act(1-act), then the adjoint terms
-            const float2 th = tanh2(fma2(sl2[r][k], vp2, nm2[r][k]));
-            const float2 act = fma2(half2, th, half2);
-            const float2 sp = mul2(act, fma2(nhalf2, th, half2));
-            const float2 dz = mul2(fma2(an2[k], we2[r][k], mul2(ad2[k], wp2[r][k])), sp);
-            Gwe[r][k] = fma2(an2[k], act, Gwe[r][k]);
-            Gwp[r][k] = fma2(ad2[k], act, Gwp[r][k]);
+            // Tanh space: with tn = tanh(-z/2) = -t and the stored a' = -a/4,
+            //   dL/dz = (a_n w_erev + a_d w_pos) act(1-act) = (a'_n w_erev + a'_d w_pos)(tn^2 - 1)
+            //   a act  = a/2 + 2 a' tn   (the a/2 part is summed per column by the tails)
+            const float2 tn = tanh2(fma2(sl2[r][k], vp2, nm2[r][k]));
+            const float2 dz = mul2(fma2(an2[k], we2[r][k], mul2(ad2[k], wp2[r][k])), fma2(tn, tn, m1));
+            Gwe[r][k] = fma2(an2[k], tn, Gwe[r][k]);
+            Gwp[r][k] = fma2(ad2[k], tn, Gwp[r][k]);
             Gdz[r][k] = add2(Gdz[r][k], dz);
             Gdzv[r][k] = fma2(dz, vp2, Gdzv[r][k]);
             dv = fma2(dz, sl2[r][k], dv);
@@ -440,7 +444,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       const int s = blk * kSB + osmp;
       if (pvalid && writer && s < nvalid) {
         const int idx = s * LDV + p;
-        float gval = fmaf(2.0f, acc[0][0], DIR[idx]);  // dL/dv_n[p] (sl holds sigma/2)
+        float gval = fmaf(-2.0f, acc[0][0], DIR[idx]);  // dL/dv_n[p] (sl holds -sigma/2)
         const long long bs = b0 + s;
         bool done = false;
         if (k == 0) {
@@ -481,19 +485,21 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     }
   // per-neuron sums: each lane holds the partial of its own row; fixed-order sum
   // over the lanes of the group through shared memory.
-  for (int i = tid; i < 3 * HP * TPC; i += NT) red[i] = 0.f;
+  for (int i = tid; i < 5 * HP * TPC; i += NT) red[i] = 0.f;
   __syncthreads();
   if (writer) {
     red[(0 * HP + p) * TPC + g] = gcm;
     red[(1 * HP + p) * TPC + g] = ggl;
     red[(2 * HP + p) * TPC + g] = gvl;
+    red[(3 * HP + p) * TPC + g] = san;
+    red[(4 * HP + p) * TPC + g] = sad;
   }
   __syncthreads();
   if (tid < G::NEUR) {
     const int row = nb + tid;
-    float* pn = a.partn + (long long)grp * 3 * HP;
+    float* pn = a.partn + (long long)grp * 5 * HP;
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
+    for (int k = 0; k < 5; ++k) {
       float sum = 0.f;
       for (int l = 0; l < TPC; ++l) sum += red[(k * HP + row) * TPC + l];
       pn[k * HP + row] = sum;
@@ -569,7 +575,7 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   // each kernel: an equal share of sample blocks per resident sample group
   // shared-memory bound of the backward kernel (13 per-sample slabs + the reduction area)
   const size_t smem_cap = 227 * 1024 - 1024;
-  const int max_per = (int)((smem_cap - 3 * HP * (HP / 8) * sizeof(float)) / (13 * LDV * sizeof(float) * kSB));
+  const int max_per = (int)((smem_cap - 5 * HP * (HP / 8) * sizeof(float)) / (13 * LDV * sizeof(float) * kSB));
   auto share = [&](int groups_per_pass) {
     int per = (blocks + groups_per_pass - 1) / groups_per_pass;
     if (per > max_per) per = max_per;
@@ -585,7 +591,8 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   p.threads_bwd = HP * HP / 8 / CL / (h64 ? LTC_BWD_RPT : 1);
   p.slots_bwd = p.grid_bwd / CL;
   p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
-  p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 3 * HP * (HP / 8)) * sizeof(float);
+  p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 5 * HP * (HP / 8)) * sizeof(float);
+  p.tanh_space = true;
   return p;
 }
 
