@@ -435,7 +435,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   sa.part = b.spart; sa.rows = L.rows; sa.D = dims->D; sa.H = dims->H; sa.HP = HP; sa.nsplit = L.sp.nsplit;
   {
     TimedLaunch tl(LTC_KERNEL_SENSORY_BWD, st);
-    e = launch_sensory_bwd(sa, L.sp, b.dxpart, st);
+    e = launch_sensory_bwd(sa, L.sp, b.dxpart, L.rp.tanh_space, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sensory_bwd");
 

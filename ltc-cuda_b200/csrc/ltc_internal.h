@@ -75,7 +75,9 @@ struct SensBwdPlan {
   size_t dxpart_floats;  // 0 when nqc == 1
 };
 SensBwdPlan plan_sensory_bwd(long long rows, int D, int HP, int num_sms);
-cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart,
+// tanh_space: the sensory partials are sums of a'*tanh and the finish kernel adds the
+// column sums of g_sn, g_sd taken from the recurrent per-neuron partials (rows 3, 4)
+cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart, bool tanh_space,
                                cudaStream_t st);
 
 // ---- recurrent forward / backward ----------------------------------------

@@ -125,6 +125,16 @@ __global__ void finish_kernel(FinishArgs a) {
         dz += base[2 * slab];
         dzx += base[3 * slab];
       }
+      if (a.rec_tanh_space) {
+        // sum g*act = sum g/2 + 2 * sum a'*tanh; sum over rows of g_sn = sum of a_n
+        float san = 0.f, sad = 0.f;
+        for (int c = 0; c < a.rslots; ++c) {
+          san += a.rec_partn[((long long)c * 5 + 3) * a.HP + q];
+          sad += a.rec_partn[((long long)c * 5 + 4) * a.HP + q];
+        }
+        an = fmaf(0.5f, san, 2.0f * an);
+        ad = fmaf(0.5f, sad, 2.0f * ad);
+      }
       a.g_serev[k] = a.sw[k] * an;
       a.g_sw[k] = a.serev[k] * an + ad;
       a.g_smu[k] = -a.ssig[k] * dz;

@@ -107,7 +107,11 @@ struct SensBwdGeom {
 // Thread = (input pair c, lane g): inputs d_r = d0 + c + r*NGD (r < 2), columns
 // q0 + sub(j, g).  The per-row adjoint loads (8 columns of gsn, gsd) are shared
 // by the two inputs.
-template <int QC>
+// TS (tanh space): the recurrent backward also produced the column sums of g_sn,
+// g_sd (= sum of a_n, a_d); the gate is evaluated as tn = tanh(-z/2) = -t, the
+// staged adjoints are scaled to a' = -g/4, and the finish kernel adds the g/2 part
+// of sum g*act:  dL/dz = (a'_n swe + a'_d sw)(tn^2 - 1),  g act = g/2 + 2 a' tn.
+template <int QC, bool TS>
 __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc, long long rows_per_split,
                                                           float* dxpart) {
   using G = SensBwdGeom<QC>;
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
       const int d = d0 + c + r * NGD;
       float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
       if (d < D) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
-      sl[r][j] = pk.x; nm[r][j] = pk.y; sw[r][j] = pk.z; swe[r][j] = pk.w;
+      sl[r][j] = TS ? -pk.x : pk.x; nm[r][j] = TS ? -pk.y : pk.y; sw[r][j] = pk.z; swe[r][j] = pk.w;
       An[r][j] = Ad[r][j] = Dz[r][j] = Dzx[r][j] = 0.f;
     }
   const int own = LR::own_base(lane);
@@ -151,8 +155,9 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
       const int r = i / QC, cc = i % QC;
       const bool ok = r < nr && cc < hq;
       const long long src = (rt + r) * H + q0 + cc;
-      GN[r * LDG + cc] = ok ? a.gsn[src] : 0.f;
-      GD[r * LDG + cc] = ok ? a.gsd[src] : 0.f;
+      const float sc = TS ? -0.25f : 1.0f;
+      GN[r * LDG + cc] = ok ? sc * a.gsn[src] : 0.f;
+      GD[r * LDG + cc] = ok ? sc * a.gsd[src] : 0.f;
     }
     for (int i = tid; i < kRT * DPC; i += NT) {
       const int r = i / DPC, cc = i % DPC;
@@ -176,19 +181,42 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const float xv = XS[row * DPC + c + r * NGD];
-          float dxs = 0.f;
+          if constexpr (TS) {
+            // synapses j, j+1 as packed f32x2 pairs
+            const float2 x2 = make_float2(xv, xv), m1 = make_float2(-1.f, -1.f);
+            float2 dxs = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float act = gate_tanh(sl[r][j], nm[r][j], xv);
-            const float sp = fmaf(-act, act, act);
-            const float dz = fmaf(an8[j], swe[r][j], ad8[j] * sw[r][j]) * sp;
-            An[r][j] = fmaf(an8[j], act, An[r][j]);
-            Ad[r][j] = fmaf(ad8[j], act, Ad[r][j]);
-            Dz[r][j] += dz;
-            Dzx[r][j] = fmaf(dz, xv, Dzx[r][j]);
-            dxs = fmaf(dz, sl[r][j], dxs);
+            for (int k = 0; k < 4; ++k) {
+              const int j = 2 * k;
+              const float2 sl2 = make_float2(sl[r][j], sl[r][j + 1]), nm2 = make_float2(nm[r][j], nm[r][j + 1]);
+              const float2 an2 = make_float2(an8[j], an8[j + 1]), ad2 = make_float2(ad8[j], ad8[j + 1]);
+              const float2 tn = tanh2(fma2(sl2, x2, nm2));
+              const float2 dz = mul2(fma2(an2, make_float2(swe[r][j], swe[r][j + 1]),
+                                          mul2(ad2, make_float2(sw[r][j], sw[r][j + 1]))),
+                                     fma2(tn, tn, m1));
+              float2 t;
+              t = fma2(an2, tn, make_float2(An[r][j], An[r][j + 1])); An[r][j] = t.x; An[r][j + 1] = t.y;
+              t = fma2(ad2, tn, make_float2(Ad[r][j], Ad[r][j + 1])); Ad[r][j] = t.x; Ad[r][j + 1] = t.y;
+              t = add2(dz, make_float2(Dz[r][j], Dz[r][j + 1])); Dz[r][j] = t.x; Dz[r][j + 1] = t.y;
+              t = fma2(dz, x2, make_float2(Dzx[r][j], Dzx[r][j + 1])); Dzx[r][j] = t.x; Dzx[r][j + 1] = t.y;
+              dxs = fma2(dz, sl2, dxs);
+            }
+            acc[0][r * kSB + i] = dxs.x + dxs.y;
+          } else {
+            float dxs = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float act = gate_tanh(sl[r][j], nm[r][j], xv);
+              const float sp = fmaf(-act, act, act);
+              const float dz = fmaf(an8[j], swe[r][j], ad8[j] * sw[r][j]) * sp;
+              An[r][j] = fmaf(an8[j], act, An[r][j]);
+              Ad[r][j] = fmaf(ad8[j], act, Ad[r][j]);
+              Dz[r][j] += dz;
+              Dzx[r][j] = fmaf(dz, xv, Dzx[r][j]);
+              dxs = fmaf(dz, sl[r][j], dxs);
+            }
+            acc[0][r * kSB + i] = dxs;
           }
-          acc[0][r * kSB + i] = dxs;
         }
       }
       LR::template run<1>(acc, lane);
@@ -199,7 +227,7 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
           const int row = blk * kSB + item % kSB;
           const int d = d0 + c + (item / kSB) * NGD;
           if (row < nr && d < D) {
-            const float v = 2.0f * acc[0][o];  // sl holds sigma/2
+            const float v = (TS ? -2.0f : 2.0f) * acc[0][o];  // sl holds (-)sigma/2
             const long long idx = (rt + row) * D + d;
             if (nqc == 1) a.dx[idx] = v;
             else dxpart[qc * ndx + idx] = v;
@@ -262,19 +290,27 @@ SensBwdPlan plan_sensory_bwd(long long rows, int D, int HP, int num_sms) {
   return p;
 }
 
-cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart, cudaStream_t st) {
+cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart, bool tanh_space,
+                               cudaStream_t st) {
   if (a.rows <= 0) return cudaSuccess;
   long long rps = (a.rows + p.nsplit - 1) / p.nsplit;
   rps = (rps + kRT - 1) / kRT * kRT;
   dim3 grid(p.ndc * p.nqc, p.nsplit);
   const size_t smem = (size_t)2 * kRT * (p.qc + 4) * 4 + (size_t)kRT * p.dpc * 4;
   cudaError_t e;
-#define LTC_SB_CASE(QCV)                                                                          \
-  case QCV:                                                                                       \
-    e = cudaFuncSetAttribute(sens_bwd_kernel<QCV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)smem);                                                         \
-    if (e != cudaSuccess) return e;                                                               \
-    sens_bwd_kernel<QCV><<<grid, 256, smem, st>>>(a, p.nqc, rps, dxpart);                         \
+#define LTC_SB_CASE(QCV)                                                                                 \
+  case QCV:                                                                                              \
+    if (tanh_space) {                                                                                    \
+      e = cudaFuncSetAttribute(sens_bwd_kernel<QCV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                               (int)smem);                                                              \
+      if (e != cudaSuccess) return e;                                                                    \
+      sens_bwd_kernel<QCV, true><<<grid, 256, smem, st>>>(a, p.nqc, rps, dxpart);                       \
+    } else {                                                                                             \
+      e = cudaFuncSetAttribute(sens_bwd_kernel<QCV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,\
+                               (int)smem);                                                              \
+      if (e != cudaSuccess) return e;                                                                    \
+      sens_bwd_kernel<QCV, false><<<grid, 256, smem, st>>>(a, p.nqc, rps, dxpart);                      \
+    }                                                                                                    \
     break;
   switch (p.qc) {
     LTC_SB_CASE(32)
