@@ -94,6 +94,80 @@ __global__ void __launch_bounds__(512, 2) sens_fwd_kernel(SensFwdArgs a) {
   }
 }
 
+// Resident variant for small sensory matrices (D*HPW float4 <= kResidentBytes): the
+// whole gate pack stays in shared memory for the kernel's lifetime, the per-column
+// weight sums are computed once, and the x tiles ([d][row], transposed) are
+// double-buffered with cp.async so their loads overlap the previous tile's gates.
+constexpr size_t kResidentBytes = 144 * 1024;
+
+template <int HPW>
+__global__ void __launch_bounds__(512, 1) sens_fwd_resident(SensFwdArgs a) {
+  constexpr int RG = 512 / HPW, TR = RG * kRB;
+  extern __shared__ __align__(16) float smem[];
+  const int D = a.D, H = a.H;
+  float4* pks = reinterpret_cast<float4*>(smem);  // [D][HPW]
+  float* xs = smem + 4 * D * HPW;                 // [2][D][TR]
+  const int tid = threadIdx.x;
+  const int q = tid % HPW, rg = tid / HPW;
+  const long long ntiles = (a.rows + TR - 1) / TR;
+
+  auto stage_x = [&](long long tile, int buf) {
+    float* dst = xs + buf * D * TR;
+    const long long row0 = tile * TR;
+    for (int i = tid; i < TR * D; i += 512) {
+      const int r = i % TR, d = i / TR;  // consecutive lanes -> consecutive rows: conflict-free stores
+      const long long row = row0 + r;
+      if (row < a.rows) cp_async4(dst + d * TR + r, a.x + row * D + d);
+      else dst[d * TR + r] = 0.f;
+    }
+    cp_async_commit();
+  };
+  for (int i = tid; i < D * HPW; i += 512) cp_async16(pks + i, a.spack + i);
+  long long tile = blockIdx.x;
+  if (tile < ntiles) stage_x(tile, 0);
+  cp_async_wait_all();
+  __syncthreads();
+  float cswe = 0.f, csw = 0.f;  // act = 0.5 + 0.5 tanh: sum_d w / 2 is added at the end
+  for (int d = 0; d < D; ++d) {
+    const float4 w = pks[d * HPW + q];
+    cswe += w.w;
+    csw += w.z;
+  }
+  int buf = 0;
+  for (; tile < ntiles; tile += gridDim.x, buf ^= 1) {
+    if (tile + gridDim.x < ntiles) stage_x(tile + gridDim.x, buf ^ 1);
+    float sn[kRB], sd[kRB];
+#pragma unroll
+    for (int r = 0; r < kRB; ++r) sn[r] = sd[r] = 0.f;
+    const float* xr = xs + buf * D * TR + rg * kRB;
+#pragma unroll 2
+    for (int d = 0; d < D; ++d) {
+      const float4 w = pks[d * HPW + q];
+      const float4 x0 = *reinterpret_cast<const float4*>(xr + d * TR);
+      const float4 x1 = *reinterpret_cast<const float4*>(xr + d * TR + 4);
+      const float xv[kRB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int r = 0; r < kRB; ++r) {
+        const float th = tanh_approx(fmaf(w.x, xv[r], w.y));
+        sn[r] = fmaf(w.w, th, sn[r]);
+        sd[r] = fmaf(w.z, th, sd[r]);
+      }
+    }
+    if (q < H) {
+#pragma unroll
+      for (int r = 0; r < kRB; ++r) {
+        const long long row = tile * TR + rg * kRB + r;
+        if (row < a.rows) {
+          a.sn[row * H + q] = 0.5f * (cswe + sn[r]);
+          a.sd[row * H + q] = 0.5f * (csw + sd[r]);
+        }
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+  }
+}
+
 template <int QC>
 struct SensBwdGeom {
   static constexpr int NT = 256;         // threads
@@ -263,6 +337,25 @@ int pick_qc(int HP) {
 
 cudaError_t launch_sensory_fwd(const SensFwdArgs& a, int num_sms, cudaStream_t st) {
   if (a.rows <= 0) return cudaSuccess;
+  const int TRr = (512 / (a.HP > 0 ? a.HP : 1)) * kRB;
+  const size_t smem_res = (size_t)a.D * a.HP * 16 + (size_t)2 * a.D * TRr * 4;
+  if ((a.HP == 32 || a.HP == 64) && (size_t)a.D * a.HP * 16 <= kResidentBytes && smem_res <= 220 * 1024) {
+    const int TR = TRr;
+    const size_t smem = smem_res;
+    const long long ntiles = (a.rows + TR - 1) / TR;
+    const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
+    cudaError_t e;
+    if (a.HP == 64) {
+      e = cudaFuncSetAttribute(sens_fwd_resident<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      sens_fwd_resident<64><<<grid, 512, smem, st>>>(a);
+    } else {
+      e = cudaFuncSetAttribute(sens_fwd_resident<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      sens_fwd_resident<32><<<grid, 512, smem, st>>>(a);
+    }
+    return cudaGetLastError();
+  }
   const SensFwdGeom G = sens_fwd_geom(a.HP, a.D);
   const size_t smem = (size_t)G.DC * G.HPW * 16 + (size_t)G.DC * G.TR * 4;
   cudaError_t e = cudaFuncSetAttribute(sens_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
