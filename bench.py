@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the configuration's global batch (profiling captures of smaller cases)")
     ap.add_argument("--seq", type=int, default=None, help="override the sequence length T (profiling captures)")
+    ap.add_argument("--graph", type=int, default=None,
+                    help="1 (default): replay the whole step as a captured CUDA graph; 0: eager launches")
     return ap.parse_args()
 
 
@@ -223,7 +225,8 @@ def main():
     model.load_state_dict(p)
     model = model.to(dev)
     bucket = FlatGradBucket(model.parameters())
-    opt = torch.optim.Adam(model.parameters(), lr=1e-4, fused=True)
+    use_graph = bool(args.graph) if args.graph is not None else True
+    opt = torch.optim.Adam(model.parameters(), lr=1e-4, fused=True, capturable=use_graph)
     x_host = x_full[lo:hi].contiguous().pin_memory()
     x_dev = x_host.to(dev)
     del x_full
@@ -254,10 +257,50 @@ def main():
         step(x_dev)
     torch.cuda.synchronize()
 
+    # CUDA-graph mode: the whole step (module forward, backward, all-reduce, Adam) is
+    # captured once per input buffer and replayed; the same kernels run, without the
+    # host launch overhead that dominates the small configurations.
+    graphs = {}
+    launches_per_step = None
+
+    def capture(xbuf):
+        nonlocal launches_per_step
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step(xbuf)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        n_before = ltc_cuda.launch_count()
+        with torch.cuda.graph(g):
+            out = step(xbuf)
+        launches_per_step = ltc_cuda.launch_count() - n_before
+        graphs[xbuf.data_ptr()] = (g, out)
+
+    def run(xbuf):
+        if not use_graph:
+            return step(xbuf)
+        g, out = graphs[xbuf.data_ptr()]
+        g.replay()
+        return out
+
+    graph_note = None
+    if use_graph:
+        try:
+            capture(x_dev)
+            for _ in range(3):
+                run(x_dev)
+            torch.cuda.synchronize()
+        except Exception as exc:  # capture unsupported here: measure eagerly and say so
+            graphs.clear()
+            use_graph = False
+            graph_note = f"graph capture failed, eager launches: {type(exc).__name__}: {exc}"[:200]
+
     # ---- device-resident timed region ----
     clocks = ClockSampler(physical_gpu_index(local))
     clocks.start()
-    ltc_cuda.timing_enable(True)
+    ltc_cuda.timing_enable(not use_graph)
     n0 = ltc_cuda.launch_count()
     barrier()
     torch.cuda.synchronize()
@@ -265,11 +308,18 @@ def main():
     ev0.record()
     for _ in range(args.steps):
         flush.zero_()
-        step(x_dev)
+        run(x_dev)
     ev1.record()
     torch.cuda.synchronize()
     barrier()
-    launches = ltc_cuda.launch_count() - n0
+    launches = (launches_per_step * args.steps) if use_graph else (ltc_cuda.launch_count() - n0)
+    if use_graph:
+        # per-kernel event times need host-side launches: one eager window of the same step
+        ltc_cuda.timing_enable(True)
+        for _ in range(args.steps):
+            flush.zero_()
+            step(x_dev)
+        torch.cuda.synchronize()
     ktimes = ltc_cuda.timing_collect()
     ltc_cuda.timing_enable(False)
     clk = clocks.stop()
@@ -284,6 +334,11 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     copy_stream = torch.cuda.Stream(dev)
     bufs = [torch.empty_like(x_dev), torch.empty_like(x_dev)]
+    if use_graph:
+        for bf in bufs:
+            bf.copy_(x_dev)
+            capture(bf)
+        torch.cuda.synchronize()
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     free = [torch.cuda.Event(), torch.cuda.Event()]
     compute = torch.cuda.current_stream(dev)
@@ -304,7 +359,7 @@ def main():
             upload(k + 1)
         flush.zero_()
         compute.wait_event(ready[k % 2])
-        loss = step(bufs[k % 2])
+        loss = run(bufs[k % 2])
         free[k % 2].record(compute)
         float(loss.item())
     e1.record()
@@ -341,7 +396,8 @@ def main():
                    "density": cfg.density, "sensory_density": cfg.sensory_density,
                    "step": "train (fwd+bwd+allreduce+adam)" if cfg.training_step else "fwd+bwd",
                    "parallelism": f"dp{world}", "per_rank_batch": Bl,
-                   "l2": "256 MB flush write between steps (inside the timed region)"},
+                   "l2": "256 MB flush write between steps (inside the timed region)",
+                   "cuda_graph": use_graph if graph_note is None else graph_note},
         "e2e": e2e,
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
                      "frac": achieved / peak,
@@ -351,6 +407,8 @@ def main():
                      "peak_basis": f"{sms} SMs x 16 MUFU/clk / 2 MUFU per visit at sm_max {f_mhz:.0f} MHz ({peaks_kind})",
                      "step_frac_survey_convention": t_roof / (ms / 1e3)},
         "kernels": kernels,
+        "kernels_source": "eager window of the same step (graph replay has no host launches)" if use_graph
+                          else "timed region",
         "gpu_launches": launches,
         "clocks": clk,
     }
@@ -359,7 +417,14 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        # Every rank has finished its device work (max-over-ranks reductions above);
+        # captured graphs hold NCCL work, and tearing the communicator down under them
+        # can block, so the ranks leave without a teardown once the line is out.
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 if __name__ == "__main__":
