@@ -187,8 +187,8 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
     __syncthreads();
     for (int u = 0; u < U; ++u) {
       const long long n = (long long)t * U + u;
-      const float* vc = vbuf + cur * ns * LDV;
-      float* vn = vbuf + (cur ^ 1) * ns * LDV;
+      const float* __restrict__ vc = vbuf + cur * ns * LDV;
+      float* __restrict__ vn = vbuf + (cur ^ 1) * ns * LDV;
       for (int blk = 0; blk < nblk; ++blk) {
         float acc[2][G::NI];
 #pragma unroll
