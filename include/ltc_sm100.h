@@ -102,6 +102,38 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
                  const float* grad_outputs, const int64_t go_strides[3], const float* grad_state,
                  const LtcGrads* grads, void* workspace, size_t workspace_bytes, ltc_stream_t stream);
 
+/* Step-level calls for callers that drive the time loop themselves; they replace the
+ * reference's per-step exports (csrc/ltc_kernels.cu:675-950, bound at :1308-1311).
+ * dims: B, H (and D for the sensory calls, ode_unfolds/epsilon for the unfold calls);
+ * T is ignored (one step).  Matrices untransposed as in LtcParams (only the fields
+ * a call uses must be set).  Each call needs a workspace of
+ * ltc_step_workspace_bytes(dims, kind) bytes, kind = 0 sensory forward, 1 unfold
+ * forward, 2 sensory backward, 3 unfold backward. */
+int ltc_step_workspace_bytes(const LtcDims* dims, int kind, size_t* bytes);
+/* ltc_sensory_fwd (csrc/ltc_kernels.cu:675): inputs (B,D) -> w_num, w_den (B,H). */
+int ltc_step_sensory_forward(const LtcDims* dims, const LtcParams* params, const float* inputs, float* w_num,
+                             float* w_den, void* workspace, size_t workspace_bytes, ltc_stream_t stream);
+/* ltc_ode_unfold_fwd (csrc/ltc_kernels.cu:716): ode_unfolds implicit-Euler unfolds from
+ * state (B,H) with the step's sensory sums; v_buffer (ode_unfolds,B,H), the input of
+ * every unfold, may be NULL. */
+int ltc_step_unfold_forward(const LtcDims* dims, const LtcParams* params, const float* state, const float* w_num,
+                            const float* w_den, float* state_out, float* v_buffer, void* workspace,
+                            size_t workspace_bytes, ltc_stream_t stream);
+/* ltc_sensory_bwd (csrc/ltc_kernels.cu:780): gradients of the sensory sums -> grad of
+ * inputs (B,D) and of sensory sigma, mu, w_pos, erev (D,H). */
+int ltc_step_sensory_backward(const LtcDims* dims, const LtcParams* params, const float* grad_w_num,
+                              const float* grad_w_den, const float* inputs, float* grad_inputs, float* g_sigma,
+                              float* g_mu, float* g_w_pos, float* g_erev, void* workspace, size_t workspace_bytes,
+                              ltc_stream_t stream);
+/* ltc_ode_unfold_bwd (csrc/ltc_kernels.cu:845): from v_buffer (ode_unfolds,B,H) and
+ * dL/d(final state) (B,H) -> dL/d(initial state), dL/d(w_num, w_den) (B,H) and the
+ * recurrent-parameter gradients.  The step's unfolds are recomputed from v_buffer[0]. */
+int ltc_step_unfold_backward(const LtcDims* dims, const LtcParams* params, const float* v_buffer, const float* w_num,
+                             const float* w_den, const float* grad_output, float* grad_v, float* grad_w_num,
+                             float* grad_w_den, float* g_w_pos, float* g_w_erev, float* g_mu, float* g_sigma,
+                             float* g_cm, float* g_gleak, float* g_vleak, void* workspace, size_t workspace_bytes,
+                             ltc_stream_t stream);
+
 /* Module preamble, fused (replaces the PyTorch ops of ltc.py:259 and ltc.py:266):
  *   y = (LayerNorm(x) * ln_w + ln_b) * in_w + in_b     over the last dim D <= 1024,
  * biased variance, eps as nn.LayerNorm.  x, y: (rows, D); stats: (rows, 2) =

@@ -459,3 +459,218 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Step-level calls: the reference's per-step exports (csrc/ltc_kernels.cu:675-950),
+// built from the same kernels with T = 1.
+// ---------------------------------------------------------------------------
+namespace {
+
+int step_layout(const LtcDims* d, int kind, Layout* L, DeviceInfo* di) {
+  if (!d) return fail("dims is NULL");
+  if (d->B < 1 || d->H < 1 || d->H > 512) return fail("invalid step dims: B=%d H=%d", d->B, d->H);
+  if ((kind == 0 || kind == 2) && d->D < 1) return fail("invalid step dims: D=%d", d->D);
+  if ((kind == 1 || kind == 3) && d->ode_unfolds < 1) return fail("invalid step dims: ode_unfolds=%d", d->ode_unfolds);
+  int err = 0;
+  *di = device_info(&err);
+  if (err) return 1;
+  if (di->major != 10) return fail("libltc_sm100 requires an sm_100 (B200-class) GPU");
+  L->rp = plan_recurrent(d->B, d->H, di->sms, d->flags & LTC_FLAG_FORCE_WIDE);
+  L->rows = d->B;
+  L->sp = plan_sensory_bwd(L->rows, d->D > 0 ? d->D : 1, L->rp.HP, di->sms);
+  L->saved_floats_v = (size_t)(d->ode_unfolds + 1) * d->B * d->H;
+  L->saved_floats_r = (size_t)d->ode_unfolds * d->B * d->H;
+  return 0;
+}
+
+struct StepBuffers {
+  float4 *pack, *packT, *spack, *nrn;
+  float *V, *R, *out, *rpart, *rpartn, *spart, *dxpart, *scratch_f, *scratch_b;
+};
+
+size_t carve_step(const LtcDims* d, const Layout& L, int kind, void* ws, StepBuffers* b) {
+  Carver c(ws);
+  const int HP = L.rp.HP;
+  *b = StepBuffers{};
+  if (kind == 0 || kind == 2) b->spack = c.take<float4>((size_t)d->D * HP);
+  if (kind == 1 || kind == 3) {
+    b->pack = c.take<float4>((size_t)HP * HP);
+    b->nrn = c.take<float4>(HP);
+    b->V = c.take<float>(L.saved_floats_v);
+    b->R = c.take<float>(L.saved_floats_r);
+    b->out = c.take<float>((size_t)d->B * d->H);
+    b->scratch_f = L.rp.scratch_fwd ? c.take<float>(L.rp.scratch_fwd) : nullptr;
+  }
+  if (kind == 3) {
+    b->packT = c.take<float4>((size_t)HP * HP);
+    b->rpart = c.take<float>((size_t)L.rp.slots_bwd * 4 * HP * HP);
+    b->rpartn = c.take<float>((size_t)L.rp.slots_bwd * 5 * HP);
+    b->scratch_b = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
+  }
+  if (kind == 2) {
+    b->spart = c.take<float>(L.sp.part_floats);
+    b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
+  }
+  return c.off + 256;
+}
+
+int step_begin(const LtcDims* d, int kind, void* ws, size_t wsb, Layout* L, DeviceInfo* di, StepBuffers* b) {
+  if (step_layout(d, kind, L, di)) return 1;
+  const size_t need = carve_step(d, *L, kind, nullptr, b);
+  if (!ws || wsb < need) return fail("step call: workspace of %zu bytes is smaller than the %zu bytes required", wsb, need);
+  carve_step(d, *L, kind, ws, b);
+  return 0;
+}
+
+// recurrent forward of one step (T = 1) from `state`, saving V/R in the workspace
+cudaError_t step_unfold_fwd(const LtcDims* d, const LtcParams* p, const Layout& L, const DeviceInfo& di,
+                            const StepBuffers& b, const float* state, const float* wn, const float* wd,
+                            cudaStream_t st) {
+  PackArgs pa = pack_args(d, p, L.rp.HP);
+  pa.ssig = nullptr;  // recurrent + per-neuron packs only
+  pa.pack = b.pack; pa.packT = b.packT; pa.nrn = b.nrn;
+  cudaError_t e = launch_pack(pa, st);
+  if (e != cudaSuccess) return e;
+  RecFwdArgs ra{};
+  ra.pack = b.pack; ra.nrn = b.nrn; ra.sn = wn; ra.sd = wd; ra.h0 = state;
+  // the final state is written twice with identical values (out after the last
+  // unfold, hT after the loop, by different threads): both go to b.out
+  ra.out = b.out; ra.hT = b.out;
+  ra.V = b.V; ra.R = b.R;
+  ra.B = d->B; ra.T = 1; ra.H = d->H; ra.U = d->ode_unfolds; ra.HP = L.rp.HP;
+  ra.ns = L.rp.ns_fwd; ra.eps = d->epsilon; ra.scratch = b.scratch_f;
+  (void)di;
+  return launch_recurrent_fwd(ra, L.rp, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltc_step_workspace_bytes(const LtcDims* dims, int kind, size_t* bytes) {
+  Layout L;
+  DeviceInfo di;
+  StepBuffers b;
+  if (!bytes) return fail("bytes is NULL");
+  if (kind < 0 || kind > 3) return fail("kind must be 0..3");
+  if (step_layout(dims, kind, &L, &di)) return 1;
+  *bytes = carve_step(dims, L, kind, nullptr, &b);
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_step_sensory_forward(const LtcDims* dims, const LtcParams* params, const float* inputs, float* w_num,
+                             float* w_den, void* workspace, size_t workspace_bytes, ltc_stream_t stream) {
+  Layout L; DeviceInfo di; StepBuffers b;
+  if (step_begin(dims, 0, workspace, workspace_bytes, &L, &di, &b)) return 1;
+  if (!params || !params->sensory_sigma || !params->sensory_mu || !params->sensory_w_pos || !params->sensory_erev ||
+      !inputs || !w_num || !w_den)
+    return fail("ltc_step_sensory_forward: NULL pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  PackArgs pa = pack_args(dims, params, L.rp.HP);
+  pa.w_pos = nullptr; pa.cm = nullptr;  // sensory pack only
+  pa.spack = b.spack;
+  cudaError_t e = launch_pack(pa, st);
+  if (e == cudaSuccess) {
+    SensFwdArgs sa{};
+    sa.spack = b.spack; sa.x = inputs; sa.sn = w_num; sa.sd = w_den; sa.rows = dims->B;
+    sa.D = dims->D; sa.H = dims->H; sa.HP = L.rp.HP;
+    e = launch_sensory_fwd(sa, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ltc_step_sensory_forward");
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_step_unfold_forward(const LtcDims* dims, const LtcParams* params, const float* state, const float* w_num,
+                            const float* w_den, float* state_out, float* v_buffer, void* workspace,
+                            size_t workspace_bytes, ltc_stream_t stream) {
+  Layout L; DeviceInfo di; StepBuffers b;
+  if (step_begin(dims, 1, workspace, workspace_bytes, &L, &di, &b)) return 1;
+  if (!params || !params->w_pos || !params->w_erev || !params->mu || !params->sigma || !params->cm_t ||
+      !params->gleak_pos || !params->vleak || !state || !w_num || !w_den || !state_out)
+    return fail("ltc_step_unfold_forward: NULL pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = step_unfold_fwd(dims, params, L, di, b, state, w_num, w_den, st);
+  const size_t bh = (size_t)dims->B * dims->H * sizeof(float);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(state_out, b.out, bh, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && v_buffer)
+    e = cudaMemcpyAsync(v_buffer, b.V, bh * dims->ode_unfolds, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "ltc_step_unfold_forward");
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_step_sensory_backward(const LtcDims* dims, const LtcParams* params, const float* grad_w_num,
+                              const float* grad_w_den, const float* inputs, float* grad_inputs, float* g_sigma,
+                              float* g_mu, float* g_w_pos, float* g_erev, void* workspace, size_t workspace_bytes,
+                              ltc_stream_t stream) {
+  Layout L; DeviceInfo di; StepBuffers b;
+  if (step_begin(dims, 2, workspace, workspace_bytes, &L, &di, &b)) return 1;
+  if (!params || !params->sensory_sigma || !params->sensory_mu || !params->sensory_w_pos || !params->sensory_erev ||
+      !grad_w_num || !grad_w_den || !inputs || !grad_inputs || !g_sigma || !g_mu || !g_w_pos || !g_erev)
+    return fail("ltc_step_sensory_backward: NULL pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  PackArgs pa = pack_args(dims, params, L.rp.HP);
+  pa.w_pos = nullptr; pa.cm = nullptr;
+  pa.spack = b.spack;
+  cudaError_t e = launch_pack(pa, st);
+  if (e == cudaSuccess) {
+    SensBwdArgs sa{};
+    sa.spack = b.spack; sa.x = inputs; sa.gsn = grad_w_num; sa.gsd = grad_w_den; sa.dx = grad_inputs;
+    sa.part = b.spart; sa.rows = dims->B; sa.D = dims->D; sa.H = dims->H; sa.HP = L.rp.HP; sa.nsplit = L.sp.nsplit;
+    e = launch_sensory_bwd(sa, L.sp, b.dxpart, false, st);
+  }
+  if (e == cudaSuccess) {
+    FinishArgs fa{};
+    fa.sens_part = b.spart; fa.nsplit = L.sp.nsplit; fa.dxpart = b.dxpart; fa.nqc = L.sp.nqc; fa.rows = dims->B;
+    fa.smu = params->sensory_mu; fa.ssig = params->sensory_sigma; fa.serev = params->sensory_erev;
+    fa.sw = params->sensory_w_pos;
+    fa.g_smu = g_mu; fa.g_ssig = g_sigma; fa.g_serev = g_erev; fa.g_sw = g_w_pos; fa.g_x = grad_inputs;
+    fa.D = dims->D; fa.H = dims->H; fa.HP = L.rp.HP;
+    e = launch_finish(fa, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ltc_step_sensory_backward");
+  g_last_error.clear();
+  return 0;
+}
+
+int ltc_step_unfold_backward(const LtcDims* dims, const LtcParams* params, const float* v_buffer, const float* w_num,
+                             const float* w_den, const float* grad_output, float* grad_v, float* grad_w_num,
+                             float* grad_w_den, float* g_w_pos, float* g_w_erev, float* g_mu, float* g_sigma,
+                             float* g_cm, float* g_gleak, float* g_vleak, void* workspace, size_t workspace_bytes,
+                             ltc_stream_t stream) {
+  Layout L; DeviceInfo di; StepBuffers b;
+  if (step_begin(dims, 3, workspace, workspace_bytes, &L, &di, &b)) return 1;
+  if (!params || !params->w_pos || !params->w_erev || !params->mu || !params->sigma || !params->cm_t ||
+      !params->gleak_pos || !params->vleak || !v_buffer || !w_num || !w_den || !grad_output || !grad_v ||
+      !grad_w_num || !grad_w_den || !g_w_pos || !g_w_erev || !g_mu || !g_sigma || !g_cm || !g_gleak || !g_vleak)
+    return fail("ltc_step_unfold_backward: NULL pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // the reciprocal denominators are not part of the reference's v_buffer: recompute the
+  // step's unfolds from its first state (v_buffer[0]) and keep V, R in the workspace
+  cudaError_t e = step_unfold_fwd(dims, params, L, di, b, v_buffer, w_num, w_den, st);
+  if (e == cudaSuccess) {
+    RecBwdArgs ra{};
+    ra.pack = b.pack; ra.packT = b.packT; ra.nrn = b.nrn; ra.V = b.V; ra.R = b.R;
+    ra.gout = grad_output; ra.go_sb = dims->H; ra.go_st = 0; ra.go_sh = 1; ra.gstate = nullptr;
+    ra.gsn = grad_w_num; ra.gsd = grad_w_den; ra.gh0 = grad_v; ra.part = b.rpart; ra.partn = b.rpartn;
+    ra.B = dims->B; ra.T = 1; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = L.rp.HP; ra.ns = L.rp.ns_bwd;
+    ra.scratch = b.scratch_b;
+    e = launch_recurrent_bwd(ra, L.rp, st);
+  }
+  if (e == cudaSuccess) {
+    FinishArgs fa{};
+    fa.rec_part = b.rpart; fa.rec_partn = b.rpartn; fa.rslots = L.rp.slots_bwd;
+    fa.rec_transposed = L.rp.wide && !L.rp.streamed; fa.rec_tanh_space = L.rp.tanh_space;
+    fa.mu = params->mu; fa.sigma = params->sigma;
+    fa.g_w_pos = g_w_pos; fa.g_w_erev = g_w_erev; fa.g_mu = g_mu; fa.g_sigma = g_sigma;
+    fa.g_cm = g_cm; fa.g_gl = g_gleak; fa.g_vl = g_vleak; fa.D = 0; fa.H = dims->H; fa.HP = L.rp.HP; fa.nqc = 1;
+    e = launch_finish(fa, di.sms, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ltc_step_unfold_backward");
+  g_last_error.clear();
+  return 0;
+}
+
+}  // extern "C"

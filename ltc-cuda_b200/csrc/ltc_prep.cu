@@ -7,9 +7,10 @@ namespace ltc {
 
 // Gate packs (sh, nh, w, w*erev) with zero padding up to HP; see ltc_common.cuh.
 __global__ void pack_kernel(PackArgs a) {
-  const long long nrec = (long long)a.HP * a.HP;
-  const long long nsen = (long long)a.D * a.HP;
-  const long long total = nrec + nsen + a.HP;
+  // a null w_pos (sigma) skips the recurrent (sensory) packs: step-level calls
+  const long long nrec = a.w_pos ? (long long)a.HP * a.HP : 0;
+  const long long nsen = a.ssig ? (long long)a.D * a.HP : 0;
+  const long long total = nrec + nsen + (a.cm ? a.HP : 0);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     if (i < nrec) {
@@ -53,7 +54,9 @@ __global__ void pack_kernel(PackArgs a) {
 }
 
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st) {
-  const long long total = (long long)a.HP * a.HP + (long long)a.D * a.HP + a.HP;
+  const long long total = (a.w_pos ? (long long)a.HP * a.HP : 0) + (a.ssig ? (long long)a.D * a.HP : 0) +
+                          (a.cm ? a.HP : 0);
+  if (total == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = (int)((total + threads - 1) / threads < 4096 ? (total + threads - 1) / threads : 4096);
   pack_kernel<<<blocks, threads, 0, st>>>(a);
@@ -66,9 +69,10 @@ cudaError_t launch_pack(const PackArgs& a, cudaStream_t st) {
 //   sensory    g_serev = sw*A_n, g_sw = serev*A_n + A_d, g_smu = -ssig*DZ, g_ssig = DZX - smu*DZ
 // where S2/DZ = sum of dL/dz and S3/DZX = sum of dL/dz * (presynaptic value).
 __global__ void finish_kernel(FinishArgs a) {
-  const long long nrec = (long long)a.H * a.H;
-  const long long nneu = a.H;
-  const long long nsen = (long long)a.D * a.H;
+  // a null rec_part (sens_part) skips the recurrent (sensory) outputs: step-level calls
+  const long long nrec = a.rec_part ? (long long)a.H * a.H : 0;
+  const long long nneu = a.rec_part ? a.H : 0;
+  const long long nsen = a.sens_part ? (long long)a.D * a.H : 0;
   const long long ndx = (a.nqc > 1) ? a.rows * a.D : 0;
   const long long total = nrec + nneu + nsen + ndx;
   const long long hp2 = (long long)a.HP * a.HP;
@@ -149,8 +153,9 @@ __global__ void finish_kernel(FinishArgs a) {
 }
 
 cudaError_t launch_finish(const FinishArgs& a, int num_sms, cudaStream_t st) {
-  const long long total = (long long)a.H * a.H + a.H + (long long)a.D * a.H +
+  const long long total = (a.rec_part ? (long long)a.H * a.H + a.H : 0) + (a.sens_part ? (long long)a.D * a.H : 0) +
                           ((a.nqc > 1) ? a.rows * a.D : 0);
+  if (total == 0) return cudaSuccess;
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
   if (blocks > 8LL * num_sms) blocks = 8LL * num_sms;

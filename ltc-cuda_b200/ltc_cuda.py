@@ -80,6 +80,16 @@ EXPORTS = {
                               + [ctypes.c_size_t, ctypes.c_void_p]),
     "ltc_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams)]
                             + [ctypes.c_void_p] * 5),
+    "ltc_step_workspace_bytes": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.c_int,
+                                                 ctypes.POINTER(ctypes.c_size_t)]),
+    "ltc_step_sensory_forward": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams)]
+                                 + [ctypes.c_void_p] * 4 + [ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_step_unfold_forward": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams)]
+                                + [ctypes.c_void_p] * 6 + [ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_step_sensory_backward": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams)]
+                                  + [ctypes.c_void_p] * 9 + [ctypes.c_size_t, ctypes.c_void_p]),
+    "ltc_step_unfold_backward": (ctypes.c_int, [ctypes.POINTER(LtcDims), ctypes.POINTER(LtcParams)]
+                                 + [ctypes.c_void_p] * 15 + [ctypes.c_size_t, ctypes.c_void_p]),
     "ltc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
     "ltc_timing_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32),
                                           ctypes.c_int]),
@@ -254,6 +264,97 @@ class _CudaModule:
                                     ctypes.byref(LtcGrads(*[g.data_ptr() for g in grads])), ws.data_ptr(),
                                     pl.bwd_workspace_bytes, stream), "ltc_full_backward")
         return grads
+
+
+    # ---- step-level calls with the reference's names (csrc/ltc_kernels.cu:1308-1311) ----
+
+    @staticmethod
+    def _step(kind, dims, fn_name, params, ptrs, dev):
+        lib = _require_kernels()
+        nbytes = ctypes.c_size_t(0)
+        with torch.cuda.device(dev):
+            _check(lib.ltc_step_workspace_bytes(ctypes.byref(dims), kind, ctypes.byref(nbytes)), fn_name)
+            ws = torch.empty(max(1, nbytes.value), dtype=torch.uint8, device=dev)
+            st = torch.cuda.current_stream(dev).cuda_stream
+            _check(getattr(lib, fn_name)(ctypes.byref(dims), ctypes.byref(params), *ptrs, ws.data_ptr(),
+                                         nbytes.value, st), fn_name)
+
+    @staticmethod
+    def ltc_sensory_fwd(inputs, sensory_sigma, sensory_mu, sensory_w_pos, sensory_erev):
+        """(B,D) inputs of one step -> [w_num_sensory, w_den_sensory] (B,H)."""
+        dev = inputs.device
+        x = _as_f32(inputs, dev, "inputs")
+        B, D = x.shape
+        H = sensory_sigma.shape[1]
+        ps = {n: _as_f32(t, dev, n) for n, t in (("sensory_sigma", sensory_sigma), ("sensory_mu", sensory_mu),
+                                                  ("sensory_w_pos", sensory_w_pos), ("sensory_erev", sensory_erev))}
+        params = LtcParams(sensory_mu=ps["sensory_mu"].data_ptr(), sensory_sigma=ps["sensory_sigma"].data_ptr(),
+                           sensory_erev=ps["sensory_erev"].data_ptr(), sensory_w_pos=ps["sensory_w_pos"].data_ptr())
+        wn = torch.empty(B, H, device=dev)
+        wd = torch.empty(B, H, device=dev)
+        _CudaModule._step(0, make_dims(B, 1, D, H, 1, 0.0, _flags), "ltc_step_sensory_forward", params,
+                          [x.data_ptr(), wn.data_ptr(), wd.data_ptr()], dev)
+        return [wn, wd]
+
+    @staticmethod
+    def _rec_params(dev, w_pos, w_erev, mu, sigma, cm_t, gleak_pos, vleak):
+        ts = [_as_f32(t, dev, "param") for t in (w_pos, w_erev, mu, sigma, cm_t, gleak_pos, vleak)]
+        return ts, LtcParams(w_pos=ts[0].data_ptr(), w_erev=ts[1].data_ptr(), mu=ts[2].data_ptr(),
+                             sigma=ts[3].data_ptr(), cm_t=ts[4].data_ptr(), gleak_pos=ts[5].data_ptr(),
+                             vleak=ts[6].data_ptr())
+
+    @staticmethod
+    def ltc_ode_unfold_fwd(state, w_pos, w_erev, mu, sigma, w_num_sensory, w_den_sensory, cm_t, gleak_pos, vleak,
+                           ode_unfolds: int, epsilon: float, save_intermediates: bool):
+        """One step's unfolds -> [state (B,H), v_buffer (U,B,H) or an empty tensor]."""
+        dev = state.device
+        st_ = _as_f32(state, dev, "state")
+        B, H = st_.shape
+        ts, params = _CudaModule._rec_params(dev, w_pos, w_erev, mu, sigma, cm_t, gleak_pos, vleak)
+        wn = _as_f32(w_num_sensory, dev, "w_num_sensory")
+        wd = _as_f32(w_den_sensory, dev, "w_den_sensory")
+        out = torch.empty(B, H, device=dev)
+        vb = torch.empty(int(ode_unfolds), B, H, device=dev) if save_intermediates else None
+        _CudaModule._step(1, make_dims(B, 1, 1, H, ode_unfolds, epsilon, _flags), "ltc_step_unfold_forward",
+                          params, [st_.data_ptr(), wn.data_ptr(), wd.data_ptr(), out.data_ptr(), _ptr(vb)], dev)
+        return [out, vb if vb is not None else torch.empty(0, device=dev)]
+
+    @staticmethod
+    def ltc_sensory_bwd(grad_w_num, grad_w_den, inputs, sensory_sigma, sensory_mu, sensory_w_pos, sensory_erev):
+        """-> [grad_inputs (B,D), grad sensory_sigma, sensory_mu, sensory_w_pos, sensory_erev (D,H)]."""
+        dev = inputs.device
+        x = _as_f32(inputs, dev, "inputs")
+        B, D = x.shape
+        H = sensory_sigma.shape[1]
+        ps = [_as_f32(t, dev, "param") for t in (sensory_sigma, sensory_mu, sensory_w_pos, sensory_erev)]
+        params = LtcParams(sensory_sigma=ps[0].data_ptr(), sensory_mu=ps[1].data_ptr(),
+                           sensory_w_pos=ps[2].data_ptr(), sensory_erev=ps[3].data_ptr())
+        gn = _as_f32(grad_w_num, dev, "grad_w_num")
+        gd = _as_f32(grad_w_den, dev, "grad_w_den")
+        gx = torch.empty(B, D, device=dev)
+        outs = [torch.empty(D, H, device=dev) for _ in range(4)]
+        _CudaModule._step(2, make_dims(B, 1, D, H, 1, 0.0, _flags), "ltc_step_sensory_backward", params,
+                          [gn.data_ptr(), gd.data_ptr(), x.data_ptr(), gx.data_ptr()] + [o.data_ptr() for o in outs],
+                          dev)
+        return [gx] + outs
+
+    @staticmethod
+    def ltc_ode_unfold_bwd(v_buffer, w_pos, w_erev, mu, sigma, w_num_sensory, w_den_sensory, cm_t, gleak_pos, vleak,
+                           grad_output, ode_unfolds: int, epsilon: float):
+        """-> [grad_v, grad_w_num, grad_w_den (B,H), grad w_pos, w_erev, mu, sigma (H,H), grad cm, gleak, vleak (H)]."""
+        dev = v_buffer.device
+        vb = _as_f32(v_buffer, dev, "v_buffer")
+        _, B, H = vb.shape
+        ts, params = _CudaModule._rec_params(dev, w_pos, w_erev, mu, sigma, cm_t, gleak_pos, vleak)
+        wn = _as_f32(w_num_sensory, dev, "w_num_sensory")
+        wd = _as_f32(w_den_sensory, dev, "w_den_sensory")
+        go = _as_f32(grad_output, dev, "grad_output")
+        outs = [torch.empty(B, H, device=dev) for _ in range(3)] + [torch.empty(H, H, device=dev) for _ in range(4)] \
+            + [torch.empty(H, device=dev) for _ in range(3)]
+        _CudaModule._step(3, make_dims(B, 1, 1, H, ode_unfolds, epsilon, _flags), "ltc_step_unfold_backward",
+                          params, [vb.data_ptr(), wn.data_ptr(), wd.data_ptr(), go.data_ptr()]
+                          + [o.data_ptr() for o in outs], dev)
+        return outs
 
 
 _cuda_module = _CudaModule()

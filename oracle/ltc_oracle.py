@@ -14,6 +14,7 @@ Reference map (paths inside the reference project):
 
 * :func:`sensory_drive`   -- ``ltc.py:44-47``  (state-independent sensory term)
 * :func:`ode_step`        -- ``ltc.py:19-65``  (one timestep, U implicit-Euler unfolds)
+* :func:`unfold_loop`     -- ``ltc.py:50-63``  (the unfolds of one step, given its sensory sums)
 * :func:`forward_loop`    -- ``ltc.py:68-106`` (outer loop over T)
 * :func:`module_preamble` -- ``ltc.py:249-288`` (LayerNorm, affine map, softplus transforms)
 """
@@ -53,15 +54,27 @@ def ode_step(inputs, state, w_pos, w_erev, mu, sigma,
     presynaptic axis (dim 1 of the (B, H_pre, H_post) broadcast).
     """
     num_s, den_s = sensory_drive(inputs, sensory_mu, sensory_sigma, sensory_erev, sensory_w_pos)
+    return unfold_loop(state, w_pos, w_erev, mu, sigma, num_s, den_s, cm_t, gleak_pos, vleak,
+                       ode_unfolds, epsilon)[0]
+
+
+def unfold_loop(state, w_pos, w_erev, mu, sigma, num_s, den_s, cm_t, gleak_pos, vleak,
+                ode_unfolds: int, epsilon: float):
+    """The U implicit-Euler unfolds of one step given its sensory sums (``ltc.py:50-63``).
+
+    Returns (final state, [input state of every unfold]).
+    """
     v = state
+    inputs_of_unfolds = []
     for _ in range(ode_unfolds):
+        inputs_of_unfolds.append(v)
         act = torch.sigmoid(sigma * (v.unsqueeze(-1) - mu))
         w_num = (act * w_erev).sum(dim=1) + num_s
         w_den = (w_pos * act).sum(dim=1) + den_s
         numerator = cm_t * v + gleak_pos * vleak + w_num
         denominator = cm_t + gleak_pos + w_den
         v = numerator / (denominator + epsilon)
-    return v
+    return v, inputs_of_unfolds
 
 
 def forward_loop(x_seq, state, w_pos, w_erev, mu, sigma,
