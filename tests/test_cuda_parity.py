@@ -235,3 +235,22 @@ def test_full_c3_gradient_linearity():
         ref = 2.0 * a[k].double() + b[k].double()
         err = (ab[k].double() - ref).abs().max().item()
         assert err <= 1e-4 * ref.abs().max().item() + 1e-6, f"{k}: {err:.3e}"
+
+
+def test_streaming_inference_matches_full_sequence():
+    """Inference fast path (eval mode, no_grad, cached transforms): feeding the sequence in
+    chunks with the carried state (test_ltc_verification.py:126-140 usage) reproduces the
+    full-sequence outputs bitwise."""
+    torch.manual_seed(5)
+    m = ltc_layer.TrueLiquidTimeConstant(48, 64).cuda().eval()
+    x = torch.randn(6, 20, 48, device="cuda")
+    with torch.no_grad():
+        full, (hf, _) = m(x)
+        state, outs = None, []
+        for t0 in range(0, 20, 7):
+            # the preamble normalises each (b, t) row on its own, so chunking is exact
+            o, state = m(x[:, t0:t0 + 7], state)
+            outs.append(o)
+    assert m._cached_transforms is not None
+    assert torch.equal(torch.cat(outs, 1), full)
+    assert torch.equal(state[0], hf)
