@@ -254,3 +254,22 @@ def test_streaming_inference_matches_full_sequence():
     assert m._cached_transforms is not None
     assert torch.equal(torch.cat(outs, 1), full)
     assert torch.equal(state[0], hf)
+
+
+@pytest.mark.parametrize("B,H", [(9000, 64), (5000, 128)])
+def test_multi_wave_grid_vs_oracle(B, H):
+    """Batches beyond one wave of resident sample groups (the per-CTA sample count is
+    capped by shared memory) run as several waves; check them against the oracle."""
+    D, T, U = 8, 2, 3
+    p = synth.make_params(D, H, 0.5, 0.5, seed=B)
+    from oracle import ltc_oracle as orc
+    x = torch.randn(B, T, D, generator=torch.Generator().manual_seed(1))
+    inp = {k: v.detach() for k, v in orc.module_preamble(p, x, 1 / 30, U).items()}
+    inp["state"] = torch.randn(B, H, generator=torch.Generator().manual_seed(2)) * 0.3
+    pl = ltc_cuda.plan(ltc_cuda.make_dims(B, T, D, H, U, 1e-8))
+    assert pl.fwd_ctas > 148 or pl.bwd_ctas > 148  # really more than one wave
+    gout = torch.randn(B, T, H, generator=torch.Generator().manual_seed(3))
+    out, h, g = cuda_solver(inp, U, 1e-8, gout=gout)
+    ro, rh, rg = oracle_solver(inp, U, 1e-8, gout=gout, device="cuda", chunk=1000)
+    assert (out.cpu() - ro.cpu()).abs().max().item() < FWD_ATOL
+    assert_grads_close(g, rg, ctx=f"multi-wave B{B} H{H}")
