@@ -194,6 +194,12 @@ int ltc_timing_collect(double* total_ms, int32_t* launches, int n);
 /* Number of kernels launched through the library by this process. */
 int64_t ltc_launch_count(void);
 
+/* Number of bounded in-kernel waits (the per-unfold exchange between the CTAs
+ * of a cluster, H in 65..128) that expired on the current device since the
+ * library was loaded; 0 in a healthy process.  Synchronises with the device.
+ * Returns -1 on a CUDA error. */
+int ltc_wait_timeouts(void);
+
 /* Last error message of the calling thread ("" if none). */
 const char* ltc_last_error(void);
 

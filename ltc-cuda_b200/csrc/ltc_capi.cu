@@ -308,6 +308,12 @@ int ltc_preamble_backward(int64_t rows, int32_t D, const float* x, const float* 
   return 0;
 }
 
+int ltc_wait_timeouts(void) {
+  int n = 0;
+  if (ltc::read_wait_timeouts(&n) != 0) return -1;
+  return n;
+}
+
 int64_t ltc_launch_count(void) {
   std::lock_guard<std::mutex> lk(g_tm_mu);
   return g_tm.launches;

@@ -128,6 +128,8 @@ struct RecPlan {
 RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide);
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
 cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
+// bounded cluster waits that expired on the current device (ltc_recurrent.cu)
+int read_wait_timeouts(int* count);
 
 // ---- deterministic reductions and final gradient transforms --------------
 struct FinishArgs {

@@ -20,12 +20,16 @@
 // owns one (neuron, sample) item and runs its per-neuron "tail".
 #include <cooperative_groups.h>
 
+#include "ltc_cluster.cuh"
 #include "ltc_common.cuh"
 #include "ltc_internal.h"
 
 namespace cg = cooperative_groups;
 
 namespace ltc {
+
+// bounded cluster waits that expired (see ltc_cluster.cuh)
+__device__ int g_ltc_wait_timeouts = 0;
 
 namespace {
 
@@ -40,6 +44,9 @@ constexpr int kSB = 4;  // samples per register block
 #endif
 #ifndef LTC_BWD_RPT
 #define LTC_BWD_RPT 2
+#endif
+#ifndef LTC_BWD_RPT128
+#define LTC_BWD_RPT128 2
 #endif
 
 template <int HP, int RPT_, int CL>
@@ -63,8 +70,9 @@ __device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
 }
 
 // Cluster helpers: with CL > 1 the CTAs of a cluster share one sample group and
-// each owns HP/CL neurons; per-neuron results are stored into every CTA's shared
-// memory (DSMEM) and the unfold barrier is the hardware cluster barrier.
+// each owns HP/CL neurons; per-neuron results of an unfold are sent to every
+// CTA's shared memory with st.async and awaited on a per-slot mbarrier
+// (ltc_cluster.cuh); the hardware cluster barrier runs only at start and end.
 template <int CL>
 __device__ __forceinline__ void group_sync() {
   if constexpr (CL > 1) cg::this_cluster().sync();
@@ -75,17 +83,6 @@ __device__ __forceinline__ int group_rank() {
   if constexpr (CL > 1) return (int)cg::this_cluster().block_rank();
   else return 0;
 }
-template <int CL>
-__device__ __forceinline__ void store_all(float* local, float v) {
-  if constexpr (CL > 1) {
-    cg::cluster_group cl = cg::this_cluster();
-#pragma unroll
-    for (int r = 0; r < CL; ++r) *cl.map_shared_rank(local, r) = v;
-  } else {
-    *local = v;
-  }
-}
-
 template <int HP>
 constexpr int cluster_of() { return HP > 64 ? 4 : 1; }
 
@@ -94,7 +91,7 @@ constexpr int fwd_rpt() { return HP >= 64 ? LTC_FWD_RPT : 1; }
 template <int HP>
 constexpr int fwd_ctas() { return HP >= 64 ? LTC_FWD_CTAS : 1; }
 template <int HP>
-constexpr int bwd_rpt() { return HP >= 64 ? LTC_BWD_RPT : 1; }
+constexpr int bwd_rpt() { return HP >= 128 ? LTC_BWD_RPT128 : HP >= 64 ? LTC_BWD_RPT : 1; }
 
 template <int HP>
 __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>::NT, fwd_ctas<HP>())
@@ -166,6 +163,20 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
   const bool qvalid = q < H;
   const bool writer = LR::writer(lane);
 
+  __shared__ __align__(8) uint64_t xbar[2];  // vbuf slot arrivals (CL > 1)
+  __shared__ int xabort;
+  const uint32_t xbytes = (uint32_t)(HP * nblk * kSB * sizeof(float));
+  if constexpr (CL > 1) {
+    if (tid == 0) {
+      xabort = 0;
+      mbar_init(smem_addr(&xbar[0]), 1);
+      mbar_init(smem_addr(&xbar[1]), 1);
+      mbar_init_fence();
+      mbar_arm(smem_addr(&xbar[0]), xbytes);
+      mbar_arm(smem_addr(&xbar[1]), xbytes);
+    }
+  }
+  uint32_t xphase = 0;  // parity bit per slot
   for (int i = tid; i < 4 * ns * LDV; i += NT) smem[i] = 0.f;
   __syncthreads();
   if (a.h0) {
@@ -233,8 +244,14 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
         const float num = (cm * v + glvl) + wn;
         const float rr = rcp_approx((cmgl + wd) + a.eps);
         const float vnew = num * rr;
-        if (qvalid && writer && s < nvalid) {
-          store_all<CL>(vn + s * LDV + q, vnew);
+        const bool ok = qvalid && s < nvalid;
+        if constexpr (CL > 1) {
+          // every item of the group is sent (zeros for padding): the phase byte count
+          if (writer) st_async_all<CL>(vn + s * LDV + q, ok ? vnew : 0.f, smem_addr(&xbar[cur ^ 1]));
+        } else {
+          if (writer && ok) vn[s * LDV + q] = vnew;
+        }
+        if (writer && ok) {
           const long long bs = b0 + s;
           if (a.V) {
             a.V[(n * B + bs) * H + q] = v;
@@ -243,7 +260,14 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
           if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
         }
       }
-      group_sync<CL>();
+      if constexpr (CL > 1) {
+        const int slot = cur ^ 1;
+        mbar_wait(smem_addr(&xbar[slot]), (xphase >> slot) & 1u, &xabort, &g_ltc_wait_timeouts);
+        xphase ^= 1u << slot;
+        if (tid == 0 && n + 2 < (long long)T * U) mbar_arm(smem_addr(&xbar[slot]), xbytes);
+      } else {
+        __syncthreads();
+      }
       cur ^= 1;
     }
   }
@@ -255,6 +279,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
     a.hT[bs * H + h] = vc[s * LDV + h];
     if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[s * LDV + h];
   }
+  if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may address it
 }
 
 // Backward: reverse sweep over n = T*U-1 .. 0 with the adjoint of each unfold.
@@ -319,6 +344,20 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   const bool writer = LR::writer(lane);
   float gcm = 0.f, ggl = 0.f, gvl = 0.f, san = 0.f, sad = 0.f;
 
+  __shared__ __align__(8) uint64_t xbar[2];  // AN/AD slot arrivals (CL > 1)
+  __shared__ int xabort;
+  const uint32_t xbytes = (uint32_t)(2 * HP * nblk * kSB * sizeof(float));
+  if constexpr (CL > 1) {
+    if (tid == 0) {
+      xabort = 0;
+      mbar_init(smem_addr(&xbar[0]), 1);
+      mbar_init(smem_addr(&xbar[1]), 1);
+      mbar_init_fence();
+      mbar_arm(smem_addr(&xbar[0]), xbytes);
+      mbar_arm(smem_addr(&xbar[1]), xbytes);
+    }
+  }
+  uint32_t xphase = 0;  // parity bit per slot
   for (int i = tid; i < 13 * SL; i += NT) smem[i] = 0.f;
   __syncthreads();
 
@@ -364,25 +403,42 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     GSD[idx] = first_of_step ? ad : GSD[idx] + ad;
     DIR[idx] = an * cm;
     // the synapse pass works in tanh space: it reads a' = -a/4 (see the pass)
-    store_all<CL>(an_d + idx, -0.25f * an);
-    store_all<CL>(ad_d + idx, -0.25f * ad);
+    if constexpr (CL > 1) {
+      const uint32_t bar = smem_addr(&xbar[(an_d - AN) / SL]);
+      st_async_all<CL>(an_d + idx, -0.25f * an, bar);
+      st_async_all<CL>(ad_d + idx, -0.25f * ad, bar);
+    } else {
+      an_d[idx] = -0.25f * an;
+      ad_d[idx] = -0.25f * ad;
+    }
+  };
+  // CL > 1: a padding item (row >= H or sample >= nvalid) still completes its bytes
+  auto send_zero = [&](float* an_d, float* ad_d, int s) {
+    if constexpr (CL > 1) {
+      const int idx = s * LDV + p;
+      const uint32_t bar = smem_addr(&xbar[(an_d - AN) / SL]);
+      st_async_all<CL>(an_d + idx, 0.f, bar);
+      st_async_all<CL>(ad_d + idx, 0.f, bar);
+    }
   };
 
   // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate
-  if (pvalid && writer) {
+  if (writer) {
+    const int m = NTU - 1;
     for (int blk = 0; blk < nblk; ++blk) {
       const int s = blk * kSB + osmp;
-      if (s < nvalid) {
+      if (pvalid && s < nvalid) {
         const long long bs = b0 + s;
         float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
         if (a.gstate) gval += a.gstate[bs * H + p];
-        const int m = NTU - 1;
         prep(RS + (m % 2) * SL, VS + (m % 3) * SL, VS + ((m + 1) % 3) * SL, AN + (m % 2) * SL,
              AD + (m % 2) * SL, s, gval, true);
+      } else {
+        send_zero(AN + (m % 2) * SL, AD + (m % 2) * SL, s);
       }
     }
   }
-  group_sync<CL>();
+  if constexpr (CL == 1) __syncthreads();
 
   int t = T - 1, k = U - 1;  // n = t*U + k
   for (int n = NTU - 1; n >= 0; --n) {
@@ -394,6 +450,12 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       stage_r(n - 2);
     }
     cp_async_commit();
+    if constexpr (CL > 1) {  // adjoints of unfold n from every CTA of the group
+      const int slot = n % 2;
+      mbar_wait(smem_addr(&xbar[slot]), (xphase >> slot) & 1u, &xabort, &g_ltc_wait_timeouts);
+      xphase ^= 1u << slot;
+      if (tid == 0 && n >= 2) mbar_arm(smem_addr(&xbar[slot]), xbytes);
+    }
 
     const int c2 = n % 2, c2m = c2 ^ 1;          // slots of unfold n and n-1 (mod 2)
     const int c3 = n % 3, c3m = (n + 2) % 3;     // slots of V[n] and V[n-1] (mod 3)
@@ -442,6 +504,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       }
       LR::template run<1>(acc, lane);
       const int s = blk * kSB + osmp;
+      if (writer && !(pvalid && s < nvalid) && n > 0) send_zero(an_m, ad_m, s);
       if (pvalid && writer && s < nvalid) {
         const int idx = s * LDV + p;
         float gval = fmaf(-2.0f, acc[0][0], DIR[idx]);  // dL/dv_n[p] (sl holds -sigma/2)
@@ -462,7 +525,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       }
     }
     cp_async_wait_all();
-    group_sync<CL>();
+    __syncthreads();  // staged V/R visible to the whole CTA
     if (--k < 0) {
       k = U - 1;
       --t;
@@ -505,6 +568,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       pn[k * HP + row] = sum;
     }
   }
+  if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may address it
 }
 
 template <int CL, typename Args>
@@ -588,7 +652,7 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   p.grid_fwd = CL * ((B + p.ns_fwd - 1) / p.ns_fwd);
   p.grid_bwd = CL * ((B + p.ns_bwd - 1) / p.ns_bwd);
   p.threads_fwd = HP * HP / 8 / CL / (h64 ? LTC_FWD_RPT : 1);
-  p.threads_bwd = HP * HP / 8 / CL / (h64 ? LTC_BWD_RPT : 1);
+  p.threads_bwd = HP * HP / 8 / CL / (HP >= 128 ? LTC_BWD_RPT128 : h64 ? LTC_BWD_RPT : 1);
   p.slots_bwd = p.grid_bwd / CL;
   p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
   p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 5 * HP * (HP / 8)) * sizeof(float);
@@ -616,4 +680,10 @@ cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStre
   }
 }
 
+}  // namespace ltc
+
+namespace ltc {
+int read_wait_timeouts(int* count) {
+  return (int)cudaMemcpyFromSymbol(count, g_ltc_wait_timeouts, sizeof(int));
+}
 }  // namespace ltc

@@ -94,6 +94,7 @@ EXPORTS = {
     "ltc_timing_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32),
                                           ctypes.c_int]),
     "ltc_launch_count": (ctypes.c_int64, []),
+    "ltc_wait_timeouts": (ctypes.c_int, []),
     "ltc_last_error": (ctypes.c_char_p, []),
     "ltc_version": (ctypes.c_int, []),
 }
@@ -191,6 +192,14 @@ def timing_collect() -> dict:
 
 def launch_count() -> int:
     return int(_require_kernels().ltc_launch_count())
+
+
+def wait_timeouts() -> int:
+    """Bounded in-kernel cluster waits that expired on the current device (0 when healthy)."""
+    n = int(_require_kernels().ltc_wait_timeouts())
+    if n < 0:
+        raise RuntimeError("ltc_wait_timeouts: " + _require_kernels().ltc_last_error().decode())
+    return n
 
 
 def _params_struct(ts: Sequence[torch.Tensor]) -> LtcParams:
