@@ -387,6 +387,12 @@ def main():
     # whole-step ceiling with the survey's counting convention (4 MUFU per fwd+bwd synapse visit)
     S = cfg.D * cfg.H + cfg.U * cfg.H * cfg.H
     t_roof = cfg.B * cfg.T * S * 4 / (16 * sms * f_mhz * 1e6 * world)
+    # recurrent kernels alone, same convention (the H=128 north-star figure)
+    per_l = lambda k: ktimes[k][0] / max(1, ktimes[k][1]) / 1e3
+    t_roof_rec = Bl * cfg.T * cfg.U * cfg.H * cfg.H * 4 / (16 * sms * f_mhz * 1e6)
+    rec_frac = t_roof_rec / (per_l("recurrent_fwd") + per_l("recurrent_bwd"))
+    # sensory forward: reads x (4 D B per (b,t)), writes sn/sd (8 H B); MUFU-bound, not HBM-bound
+    sens_gbs = Bl * cfg.T * (4 * cfg.D + 8 * cfg.H) / per_l("sensory_fwd") / 1e9
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -405,7 +411,10 @@ def main():
                                  if (cfg.name, dom) in NCU_TRAFFIC_PER_BT else None),
                      "traffic_unit": "bytes per launch (ncu capture, scaled)",
                      "peak_basis": f"{sms} SMs x 16 MUFU/clk / 2 MUFU per visit at sm_max {f_mhz:.0f} MHz ({peaks_kind})",
-                     "step_frac_survey_convention": t_roof / (ms / 1e3)},
+                     "step_frac_survey_convention": t_roof / (ms / 1e3),
+                     "recurrent_frac_survey_convention": rec_frac,
+                     "sensory_fwd_hbm_gbs": sens_gbs,
+                     "sensory_fwd_hbm_frac": sens_gbs / float(peaks.get("hbm_gbs", 6650.0))},
         "kernels": kernels,
         "kernels_source": "eager window of the same step (graph replay has no host launches)" if use_graph
                           else "timed region",

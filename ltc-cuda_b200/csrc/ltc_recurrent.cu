@@ -20,6 +20,8 @@
 // owns one (neuron, sample) item and runs its per-neuron "tail".
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "ltc_cluster.cuh"
 #include "ltc_common.cuh"
 #include "ltc_internal.h"
@@ -34,6 +36,7 @@ __device__ int g_ltc_wait_timeouts = 0;
 namespace {
 
 constexpr int kSB = 4;  // samples per register block
+constexpr int kMaxBlk = 8;  // sample blocks per group of a cluster kernel (CL > 1)
 
 // Neurons per thread and resident CTAs per SM of each kernel at HP = 64 (tuned on B200).
 #ifndef LTC_FWD_RPT
@@ -163,17 +166,18 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
   const bool qvalid = q < H;
   const bool writer = LR::writer(lane);
 
-  __shared__ __align__(8) uint64_t xbar[2];  // vbuf slot arrivals (CL > 1)
+  // vbuf arrivals (CL > 1): one mbarrier per (slot, sample block), so that a
+  // block's pass starts as soon as that block's values are in, while the
+  // exchange of the other blocks is still in flight
+  __shared__ __align__(8) uint64_t xbar[2][kMaxBlk];
   __shared__ int xabort;
-  const uint32_t xbytes = (uint32_t)(HP * nblk * kSB * sizeof(float));
+  const uint32_t xbytes = (uint32_t)(HP * kSB * sizeof(float));  // per block and phase
   if constexpr (CL > 1) {
     if (tid == 0) {
       xabort = 0;
-      mbar_init(smem_addr(&xbar[0]), 1);
-      mbar_init(smem_addr(&xbar[1]), 1);
+      for (int i = 0; i < 2 * nblk; ++i) mbar_init(smem_addr(&xbar[i & 1][i >> 1]), 1);
       mbar_init_fence();
-      mbar_arm(smem_addr(&xbar[0]), xbytes);
-      mbar_arm(smem_addr(&xbar[1]), xbytes);
+      for (int i = 0; i < 2 * nblk; ++i) mbar_arm(smem_addr(&xbar[i & 1][i >> 1]), xbytes);
     }
   }
   uint32_t xphase = 0;  // parity bit per slot
@@ -201,6 +205,13 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
       const float* __restrict__ vc = vbuf + cur * ns * LDV;
       float* __restrict__ vn = vbuf + (cur ^ 1) * ns * LDV;
       for (int blk = 0; blk < nblk; ++blk) {
+        if constexpr (CL > 1) {  // this block's v of unfold n, from every CTA of the group
+          if (n > 0) {
+            const uint32_t bar = smem_addr(&xbar[cur][blk]);
+            mbar_wait(bar, (xphase >> cur) & 1u, &xabort, &g_ltc_wait_timeouts);
+            if (tid == 0 && n + 1 < (long long)T * U) mbar_arm(bar, xbytes);
+          }
+        }
         float acc[2][G::NI];
 #pragma unroll
         for (int i = 0; i < kSB; ++i) {
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
         const bool ok = qvalid && s < nvalid;
         if constexpr (CL > 1) {
           // every item of the group is sent (zeros for padding): the phase byte count
-          if (writer) st_async_all<CL>(vn + s * LDV + q, ok ? vnew : 0.f, smem_addr(&xbar[cur ^ 1]));
+          if (writer) st_async_all<CL>(vn + s * LDV + q, ok ? vnew : 0.f, smem_addr(&xbar[cur ^ 1][blk]));
         } else {
           if (writer && ok) vn[s * LDV + q] = vnew;
         }
@@ -261,15 +272,16 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
         }
       }
       if constexpr (CL > 1) {
-        const int slot = cur ^ 1;
-        mbar_wait(smem_addr(&xbar[slot]), (xphase >> slot) & 1u, &xabort, &g_ltc_wait_timeouts);
-        xphase ^= 1u << slot;
-        if (tid == 0 && n + 2 < (long long)T * U) mbar_arm(smem_addr(&xbar[slot]), xbytes);
+        if (n > 0) xphase ^= 1u << cur;
       } else {
         __syncthreads();
       }
       cur ^= 1;
     }
+  }
+  if constexpr (CL > 1) {  // the last unfold's v from every CTA of the group
+    for (int blk = 0; blk < nblk; ++blk)
+      mbar_wait(smem_addr(&xbar[cur][blk]), (xphase >> cur) & 1u, &xabort, &g_ltc_wait_timeouts);
   }
   const float* vc = vbuf + cur * ns * LDV;
   for (int i = tid; i < nvalid * G::NEUR; i += NT) {
@@ -344,17 +356,18 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   const bool writer = LR::writer(lane);
   float gcm = 0.f, ggl = 0.f, gvl = 0.f, san = 0.f, sad = 0.f;
 
-  __shared__ __align__(8) uint64_t xbar[2];  // AN/AD slot arrivals (CL > 1)
+  // AN/AD arrivals (CL > 1): one mbarrier per (slot, sample block), so that a
+  // block's pass starts as soon as that block's values are in, while the
+  // exchange of the other blocks is still in flight
+  __shared__ __align__(8) uint64_t xbar[2][kMaxBlk];
   __shared__ int xabort;
-  const uint32_t xbytes = (uint32_t)(2 * HP * nblk * kSB * sizeof(float));
+  const uint32_t xbytes = (uint32_t)(2 * HP * kSB * sizeof(float));  // per block and phase
   if constexpr (CL > 1) {
     if (tid == 0) {
       xabort = 0;
-      mbar_init(smem_addr(&xbar[0]), 1);
-      mbar_init(smem_addr(&xbar[1]), 1);
+      for (int i = 0; i < 2 * nblk; ++i) mbar_init(smem_addr(&xbar[i & 1][i >> 1]), 1);
       mbar_init_fence();
-      mbar_arm(smem_addr(&xbar[0]), xbytes);
-      mbar_arm(smem_addr(&xbar[1]), xbytes);
+      for (int i = 0; i < 2 * nblk; ++i) mbar_arm(smem_addr(&xbar[i & 1][i >> 1]), xbytes);
     }
   }
   uint32_t xphase = 0;  // parity bit per slot
@@ -404,7 +417,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     DIR[idx] = an * cm;
     // the synapse pass works in tanh space: it reads a' = -a/4 (see the pass)
     if constexpr (CL > 1) {
-      const uint32_t bar = smem_addr(&xbar[(an_d - AN) / SL]);
+      const uint32_t bar = smem_addr(&xbar[(an_d - AN) / SL][s / kSB]);
       st_async_all<CL>(an_d + idx, -0.25f * an, bar);
       st_async_all<CL>(ad_d + idx, -0.25f * ad, bar);
     } else {
@@ -416,7 +429,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   auto send_zero = [&](float* an_d, float* ad_d, int s) {
     if constexpr (CL > 1) {
       const int idx = s * LDV + p;
-      const uint32_t bar = smem_addr(&xbar[(an_d - AN) / SL]);
+      const uint32_t bar = smem_addr(&xbar[(an_d - AN) / SL][s / kSB]);
       st_async_all<CL>(an_d + idx, 0.f, bar);
       st_async_all<CL>(ad_d + idx, 0.f, bar);
     }
@@ -450,12 +463,6 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       stage_r(n - 2);
     }
     cp_async_commit();
-    if constexpr (CL > 1) {  // adjoints of unfold n from every CTA of the group
-      const int slot = n % 2;
-      mbar_wait(smem_addr(&xbar[slot]), (xphase >> slot) & 1u, &xabort, &g_ltc_wait_timeouts);
-      xphase ^= 1u << slot;
-      if (tid == 0 && n >= 2) mbar_arm(smem_addr(&xbar[slot]), xbytes);
-    }
 
     const int c2 = n % 2, c2m = c2 ^ 1;          // slots of unfold n and n-1 (mod 2)
     const int c3 = n % 3, c3m = (n + 2) % 3;     // slots of V[n] and V[n-1] (mod 3)
@@ -467,6 +474,11 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     float* an_m = AN + c2m * SL;
     float* ad_m = AD + c2m * SL;
     for (int blk = 0; blk < nblk; ++blk) {
+      if constexpr (CL > 1) {  // this block's adjoints of unfold n, from every CTA of the group
+        const uint32_t bar = smem_addr(&xbar[c2][blk]);
+        mbar_wait(bar, (xphase >> c2) & 1u, &xabort, &g_ltc_wait_timeouts);
+        if (tid == 0 && n >= 2) mbar_arm(bar, xbytes);
+      }
       float acc[1][G::NI];
 #pragma unroll
       for (int i = 0; i < kSB; ++i) {
@@ -524,6 +536,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
         if (!done) prep(rsm, vsm, vsn, an_m, ad_m, s, gval, k == 0);
       }
     }
+    if constexpr (CL > 1) xphase ^= 1u << c2;
     cp_async_wait_all();
     __syncthreads();  // staged V/R visible to the whole CTA
     if (--k < 0) {
@@ -619,6 +632,49 @@ cudaError_t launch_stream_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_
 cudaError_t launch_stream_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
 void plan_stream(RecPlan& p, int B, int H, int num_sms);
 
+namespace {
+__global__ void cluster_probe_kernel() {}
+}  // namespace
+
+// Clusters of CL CTAs (one CTA per SM) that can be resident at once on the
+// current device.  A cluster must fit in one GPC, so this is below num_sms/CL
+// when GPC sizes are not multiples of CL; planning with num_sms/CL would then
+// leave a second wave of clusters.  Cached per device.
+int resident_clusters(int CL, int num_sms) {
+  static std::mutex mu;
+  static int cache[64][2] = {};
+  int dev = 0;
+  const int fallback = num_sms / CL;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || (CL != 4 && CL != 8)) {
+    cudaGetLastError();
+    return fallback;
+  }
+  const int slot = CL == 4 ? 0 : 1;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev][slot] == 0) {
+    const int smem = 200 * 1024;  // forces one CTA per SM, like the recurrent kernels
+    int n = 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL * fallback);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaFuncSetAttribute(cluster_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, cluster_probe_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = fallback;
+    }
+    cache[dev][slot] = n < fallback ? n : fallback;
+  }
+  return cache[dev][slot];
+}
+
 RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
   RecPlan p{};
   p.HP = pad_neurons(H);
@@ -628,21 +684,28 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
     return p;
   }
   if (H > 128) {
-    plan_stream(p, B, H, num_sms);
+    plan_stream(p, B, H, 8 * resident_clusters(8, num_sms));
     return p;
   }
   const int HP = p.HP;  // 32, 64 or 128
   const int LDV = HP + 4;
   const int CL = HP > 64 ? 4 : 1;  // cluster_of<HP>()
-  const int groups = num_sms / CL;
+  const int groups = CL > 1 ? resident_clusters(CL, num_sms) : num_sms;
   const int blocks = (B + kSB - 1) / kSB;
   // each kernel: an equal share of sample blocks per resident sample group
   // shared-memory bound of the backward kernel (13 per-sample slabs + the reduction area)
   const size_t smem_cap = 227 * 1024 - 1024;
   const int max_per = (int)((smem_cap - 5 * HP * (HP / 8) * sizeof(float)) / (13 * LDV * sizeof(float) * kSB));
+  // blocks per group: as many waves of resident groups as the per-group cap
+  // forces, and the blocks spread evenly over them (a ragged last wave costs a
+  // full one)
+  const int cap = CL > 1 && max_per > kMaxBlk ? kMaxBlk : (max_per < 1 ? 1 : max_per);
   auto share = [&](int groups_per_pass) {
-    int per = (blocks + groups_per_pass - 1) / groups_per_pass;
-    if (per > max_per) per = max_per;
+    const long long per_wave = (long long)groups_per_pass * cap;
+    const long long waves = (blocks + per_wave - 1) / per_wave;
+    const long long slots = waves * groups_per_pass;
+    int per = (int)((blocks + slots - 1) / slots);
+    if (per > cap) per = cap;
     if (per < 1) per = 1;
     return per * kSB;
   };

@@ -427,13 +427,15 @@ cudaError_t launch_cluster8(void (*kernel)(Args), const Args& a, int grid, size_
 
 template <int NEUR>
 cudaError_t fwd_dispatch(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
+#define LTC_NSPT_CASE(N) \
+  case N: return launch_cluster8(rec_fwd_stream<NEUR, N>, a, p.grid_fwd, p.smem_fwd, st);
   switch (p.ns_fwd / SGeom<NEUR>::SGF) {
-    case 1: return launch_cluster8(rec_fwd_stream<NEUR, 1>, a, p.grid_fwd, p.smem_fwd, st);
-    case 2: return launch_cluster8(rec_fwd_stream<NEUR, 2>, a, p.grid_fwd, p.smem_fwd, st);
-    case 4: return launch_cluster8(rec_fwd_stream<NEUR, 4>, a, p.grid_fwd, p.smem_fwd, st);
-    case 8: return launch_cluster8(rec_fwd_stream<NEUR, 8>, a, p.grid_fwd, p.smem_fwd, st);
-    default: return launch_cluster8(rec_fwd_stream<NEUR, 16>, a, p.grid_fwd, p.smem_fwd, st);
+    LTC_NSPT_CASE(1) LTC_NSPT_CASE(2) LTC_NSPT_CASE(3) LTC_NSPT_CASE(4) LTC_NSPT_CASE(6)
+    LTC_NSPT_CASE(8) LTC_NSPT_CASE(12) LTC_NSPT_CASE(16) LTC_NSPT_CASE(18) LTC_NSPT_CASE(20)
+    LTC_NSPT_CASE(24)
+    default: return cudaErrorInvalidConfiguration;
   }
+#undef LTC_NSPT_CASE
 }
 
 }  // namespace
@@ -445,11 +447,24 @@ void plan_stream(RecPlan& p, int B, int H, int num_sms) {
   p.HP = HP;
   p.wide = true;
   p.streamed = true;
-  const int groups = num_sms / kCL;
-  const int max_nspt = NEUR == 64 ? 16 : 8;  // 64 samples per group at most
-  int want = (B + groups - 1) / groups;
-  int nspt = 1;
-  while (nspt < max_nspt && nspt * SGF < want) nspt *= 2;
+  const int groups = num_sms / kCL > 0 ? num_sms / kCL : 1;  // resident clusters
+  // samples per group: at most what the backward's shared memory holds (its
+  // staging grows by 16*QC + 8*NEUR bytes per sample), in steps of SGF samples
+  // per thread of the forward (instantiated counts kNspt); as many waves of
+  // resident clusters as that cap forces, the samples spread evenly over them
+  constexpr int kNspt[] = {1, 2, 3, 4, 6, 8, 12, 16, 18, 20, 24};
+  constexpr int kNn = sizeof(kNspt) / sizeof(kNspt[0]);
+  const long long fixed = (long long)2 * NEUR * QC * 16 + (long long)2 * 4 * NEUR * QC * 4;
+  const int ns_cap = (int)((227LL * 1024 - 1024 - fixed) / (16 * QC + 8 * NEUR));
+  int top = 0;  // largest instantiated count within the cap
+  for (int i = 0; i < kNn; ++i)
+    if (kNspt[i] * SGF <= ns_cap) top = i;
+  const long long per_wave = (long long)groups * kNspt[top] * SGF;
+  const long long waves = (B + per_wave - 1) / per_wave;
+  const int want = (int)((B + waves * groups - 1) / (waves * groups));
+  int nspt = kNspt[top];
+  for (int i = top; i >= 0; --i)
+    if (kNspt[i] * SGF >= want) nspt = kNspt[i];
   const int ns = nspt * SGF;  // a multiple of kSB
   p.ns_fwd = p.ns_bwd = ns;
   const int ngroups = (B + ns - 1) / ns;
