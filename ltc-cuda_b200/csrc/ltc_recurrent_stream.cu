@@ -31,6 +31,9 @@ constexpr int kCL = 8;    // CTAs per cluster
 constexpr int kNT = 256;  // threads per CTA
 constexpr int kPC = 32;   // presynaptic rows per forward chunk
 constexpr int kSB = 4;    // samples per register block (backward)
+constexpr int kMaxTailSamples = 96;
+constexpr int kPS = kNT + 1;  // padded pack row (float4) of the backward's chunk staging
+constexpr int kGS = kNT + 4;  // padded gradient row (float4)  // samples per group the backward's tail handles (ns cap)
 
 template <int NEUR>
 struct SGeom {
@@ -174,12 +177,15 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   const int ns = a.ns;
   // pack / gradient chunks are staged thread-major ([slot][thread]) so that each
   // thread's 8 synapses are read without bank conflicts
-  float4* pks = reinterpret_cast<float4*>(smem);        // [2][8][kNT]   (pack of synapse j)
-  float* gch = smem + 2 * 4 * NEUR * QC;                // [2][4][2][kNT] float4 (sums k, j-half)
-  float* anc = gch + 2 * 4 * NEUR * QC;                 // [2][ns][QC]
+  // pack / gradient rows are padded (kPS, kGS float4) so that the coalesced
+  // staging copies (consecutive threads = consecutive global addresses) also
+  // write shared memory without bank conflicts
+  float4* pks = reinterpret_cast<float4*>(smem);        // [2][8][kPS]   (pack of synapse j)
+  float* gch = smem + 2 * 8 * kPS * 4;                  // [2][4][2][kGS] float4 (sums k, j-half)
+  float* anc = gch + 2 * 8 * kGS * 4;                   // [2][ns][QC]
   float* adc = anc + 2 * ns * QC;                       // [2][ns][QC]
   float* DV = adc + 2 * ns * QC;                        // [ns][NEUR]
-  float* VP = DV + ns * NEUR;                           // [ns][NEUR]
+  float* VPb = DV + ns * NEUR;                          // [2][ns][NEUR]: V[m] of the own rows, slot m&1
 
   cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, lane = tid & 31;
@@ -212,6 +218,20 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
     anc[(buf * ns + s) * QC + cc] = 0.f;
     adc[(buf * ns + s) * QC + cc] = 0.f;
   }
+  // padded rows / samples of both V slots stay 0 (only valid entries are staged)
+  for (int i = tid; i < 2 * ns * NEUR; i += kNT) VPb[i] = 0.f;
+  __syncthreads();
+  auto stage_vp = [&](int m) {  // V[m] -> VPb[m&1]
+    float* dst = VPb + (m & 1) * ns * NEUR;
+    const int nr = min(NEUR, H - nb);
+    if (nr <= 0) return;
+    for (int i = tid; i < nvalid * nr; i += kNT) {
+      const int s = i / nr, r = i % nr;
+      cp_async4(dst + s * NEUR + r, a.V + ((long long)m * B + b0 + s) * H + nb + r);
+    }
+  };
+  stage_vp(NTU - 1);
+  cp_async_commit();
   // zero this CTA's rows of the gradient slab
   for (int i = tid; i < NEUR * HP; i += kNT) {
     const long long o = (long long)(nb + i / HP) * HP + i % HP;
@@ -258,17 +278,19 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   cluster.sync();
 
   auto stage = [&](int n, int c, int buf) {
-    // thread th = (row th/QL, lane th%QL) owns columns c*QC + (th%QL)*8 + j
-    float4* pd = pks + buf * 8 * kNT;
-    for (int i = tid; i < 8 * kNT; i += kNT) {
-      const int j = i / kNT, th = i % kNT;
-      cp_async16(pd + i, a.pack + (long long)(nb + th / QL) * HP + c * QC + (th % QL) * 8 + j);
+    // thread th = (row th/QL, lane th%QL) owns columns c*QC + (th%QL)*8 + j;
+    // copies walk the chunk row by row (coalesced) and scatter into that layout
+    float4* pd = pks + buf * 8 * kPS;
+    for (int i = tid; i < NEUR * QC; i += kNT) {
+      const int rw = i / QC, col = i % QC;
+      cp_async16(pd + (col % 8) * kPS + rw * QL + col / 8, a.pack + (long long)(nb + rw) * HP + c * QC + col);
     }
-    float4* gd = reinterpret_cast<float4*>(gch) + buf * 8 * kNT;
-    for (int i = tid; i < 8 * kNT; i += kNT) {
-      const int kh = i / kNT, th = i % kNT;  // kh = k*2 + half
-      const int k = kh / 2, half = kh % 2;
-      cp_async16(gd + i, slab + k * hp2 + (long long)(nb + th / QL) * HP + c * QC + (th % QL) * 8 + 4 * half);
+    float4* gd = reinterpret_cast<float4*>(gch) + buf * 8 * kGS;
+    for (int i = tid; i < NEUR * QC; i += kNT) {
+      const int k = i / (NEUR * QC / 4), rem = i % (NEUR * QC / 4);
+      const int rw = rem / (QC / 4), c4 = rem % (QC / 4);  // columns 4*c4 .. 4*c4+3
+      cp_async16(gd + (k * 2 + c4 % 2) * kGS + rw * QL + c4 / 2,
+                 slab + k * hp2 + (long long)(nb + rw) * HP + c * QC + 4 * c4);
     }
     const float* asrc = ANg + (n & 1) * SB_;
     const float* dsrc = ADg + (n & 1) * SB_;
@@ -288,11 +310,10 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   const float2 half2 = make_float2(0.5f, 0.5f), nhalf2 = make_float2(-0.5f, -0.5f);
   int t = T - 1, k = U - 1;
   for (int n = NTU - 1; n >= 0; --n) {
-    for (int i = tid; i < ns * NEUR; i += kNT) {
-      const int s = i / NEUR, r = i % NEUR;
-      DV[i] = 0.f;
-      VP[i] = (s < nvalid && nb + r < H) ? a.V[((long long)n * B + b0 + s) * H + nb + r] : 0.f;
-    }
+    for (int i = tid; i < ns * NEUR; i += kNT) DV[i] = 0.f;
+    const float* VP = VPb + (n & 1) * ns * NEUR;       // V[n], staged one unfold ahead
+    const float* VPm = VPb + ((n + 1) & 1) * ns * NEUR;  // V[n-1], staged now for the tails
+    if (n >= 1) stage_vp(n - 1);
     stage(n, 0, 0);
     for (int c = 0; c < NC; ++c) {
       cp_async_wait_all();
@@ -300,11 +321,11 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       if (c + 1 < NC) stage(n, c + 1, (c + 1) & 1);
       const int buf = c & 1;
       float2 sl2[4], nm2[4], wp2[4], we2[4], G0[4], G1[4], G2[4], G3[4];
-      const float4* pk = pks + buf * 8 * kNT + tid;
-      const float4* gs = reinterpret_cast<const float4*>(gch) + buf * 8 * kNT + tid;
+      const float4* pk = pks + buf * 8 * kPS + tid;
+      const float4* gs = reinterpret_cast<const float4*>(gch) + buf * 8 * kGS + tid;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const float4 p0 = pk[(2 * kk) * kNT], p1 = pk[(2 * kk + 1) * kNT];
+        const float4 p0 = pk[(2 * kk) * kPS], p1 = pk[(2 * kk + 1) * kPS];
         sl2[kk] = make_float2(p0.x, p1.x);
         nm2[kk] = make_float2(p0.y, p1.y);
         wp2[kk] = make_float2(p0.z, p1.z);
@@ -312,8 +333,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       }
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
-        const float4 g0 = gs[(0 + h2) * kNT], g1 = gs[(2 + h2) * kNT];
-        const float4 g2 = gs[(4 + h2) * kNT], g3 = gs[(6 + h2) * kNT];
+        const float4 g0 = gs[(0 + h2) * kGS], g1 = gs[(2 + h2) * kGS];
+        const float4 g2 = gs[(4 + h2) * kGS], g3 = gs[(6 + h2) * kGS];
         G0[2 * h2] = make_float2(g0.x, g0.y); G0[2 * h2 + 1] = make_float2(g0.z, g0.w);
         G1[2 * h2] = make_float2(g1.x, g1.y); G1[2 * h2 + 1] = make_float2(g1.z, g1.w);
         G2[2 * h2] = make_float2(g2.x, g2.y); G2[2 * h2 + 1] = make_float2(g2.z, g2.w);
@@ -359,31 +380,71 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       // write the chunk's gradient sums back to the slab (L2)
       float* gdst = slab + (long long)p * HP + c * QC + ql * 8;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        *reinterpret_cast<float2*>(gdst + 2 * kk) = G0[kk];
-        *reinterpret_cast<float2*>(gdst + hp2 + 2 * kk) = G1[kk];
-        *reinterpret_cast<float2*>(gdst + 2 * hp2 + 2 * kk) = G2[kk];
-        *reinterpret_cast<float2*>(gdst + 3 * hp2 + 2 * kk) = G3[kk];
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int k0 = 2 * h2, k1 = 2 * h2 + 1;
+        *reinterpret_cast<float4*>(gdst + 4 * h2) = make_float4(G0[k0].x, G0[k0].y, G0[k1].x, G0[k1].y);
+        *reinterpret_cast<float4*>(gdst + hp2 + 4 * h2) = make_float4(G1[k0].x, G1[k0].y, G1[k1].x, G1[k1].y);
+        *reinterpret_cast<float4*>(gdst + 2 * hp2 + 4 * h2) = make_float4(G2[k0].x, G2[k0].y, G2[k1].x, G2[k1].y);
+        *reinterpret_cast<float4*>(gdst + 3 * hp2 + 4 * h2) = make_float4(G3[k0].x, G3[k0].y, G3[k1].x, G3[k1].y);
       }
     }
     __syncthreads();
-    // per-neuron tails of the own rows
-    for (int s = ql; s < nvalid; s += QL) {
-      if (!pvalid) continue;
-      const long long bs = b0 + s;
-      const long long o = bs * HP + p;
-      float gval = fmaf(2.0f, DV[s * NEUR + rl], ldcg(DIRg + o));  // sl holds sigma/2
-      if (k == 0) {
-        const long long row = bs * T + t;
-        a.gsn[row * H + p] = ldcg(GSNg + o);
-        a.gsd[row * H + p] = ldcg(GSDg + o);
-        if (t == 0) {
-          a.gh0[bs * H + p] = gval;
-          continue;
+    // per-neuron tails of the own rows, samples s = ql + j*QL.  All global loads
+    // of the thread's samples are issued first (the chunk registers are dead
+    // here), then the math and stores run: the L2 latencies overlap instead of
+    // serialising behind the stores of the previous sample.
+    {
+      constexpr int kTS = kMaxTailSamples / QL;
+      const bool last = (k == 0 && t == 0);  // unfold 0 of step 0: only dL/dh0 remains
+      float dirv[kTS], gsnv[kTS], gsdv[kTS], rv[kTS], gov[kTS];
+#pragma unroll
+      for (int j = 0; j < kTS; ++j) {
+        const int s = ql + j * QL;
+        dirv[j] = gsnv[j] = gsdv[j] = rv[j] = gov[j] = 0.f;
+        if (s < nvalid && pvalid) {
+          const long long bs = b0 + s;
+          const long long o = bs * HP + p;
+          dirv[j] = ldcg(DIRg + o);
+          gsnv[j] = ldcg(GSNg + o);
+          gsdv[j] = ldcg(GSDg + o);
+          if (!last) rv[j] = a.R[((long long)(n - 1) * B + bs) * H + p];
+          if (k == 0 && !last) gov[j] = a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
         }
-        gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
       }
-      prep(n - 1, s, gval, k == 0);
+#pragma unroll
+      for (int j = 0; j < kTS; ++j) {
+        const int s = ql + j * QL;
+        if (s < nvalid && pvalid) {
+          const long long bs = b0 + s;
+          const long long o = bs * HP + p;
+          float gval = fmaf(2.0f, DV[s * NEUR + rl], dirv[j]);  // sl holds sigma/2
+          if (k == 0) {
+            const long long row = bs * T + t;
+            a.gsn[row * H + p] = gsnv[j];
+            a.gsd[row * H + p] = gsdv[j];
+            if (last) {
+              a.gh0[bs * H + p] = gval;
+              continue;
+            }
+            gval += gov[j];
+          }
+          // prep of unfold n-1: R[n-1], V[n-1] (VPm) and V[n] (VP)
+          const float r = rv[j];
+          const float vin = VPm[s * NEUR + rl];
+          const float vout = VP[s * NEUR + rl];
+          const float an = gval * r;
+          const float ad = -an * vout;
+          gcm = fmaf(an, vin - vout, gcm);
+          ggl = fmaf(an, vl - vout, ggl);
+          gvl = fmaf(an, gl, gvl);
+          const bool first = k == 0;
+          GSNg[o] = first ? an : gsnv[j] + an;
+          GSDg[o] = first ? ad : gsdv[j] + ad;
+          DIRg[o] = an * cm;
+          ANg[((n - 1) & 1) * SB_ + o] = an;
+          ADg[((n - 1) & 1) * SB_ + o] = ad;
+        }
+      }
     }
     cluster.sync();  // release a_n/a_d of unfold n-1 / acquire the peers'
     if (--k < 0) {
@@ -449,13 +510,14 @@ void plan_stream(RecPlan& p, int B, int H, int num_sms) {
   p.streamed = true;
   const int groups = num_sms / kCL > 0 ? num_sms / kCL : 1;  // resident clusters
   // samples per group: at most what the backward's shared memory holds (its
-  // staging grows by 16*QC + 8*NEUR bytes per sample), in steps of SGF samples
+  // staging grows by 16*QC + 12*NEUR bytes per sample), in steps of SGF samples
   // per thread of the forward (instantiated counts kNspt); as many waves of
   // resident clusters as that cap forces, the samples spread evenly over them
   constexpr int kNspt[] = {1, 2, 3, 4, 6, 8, 12, 16, 18, 20, 24};
   constexpr int kNn = sizeof(kNspt) / sizeof(kNspt[0]);
-  const long long fixed = (long long)2 * NEUR * QC * 16 + (long long)2 * 4 * NEUR * QC * 4;
-  const int ns_cap = (int)((227LL * 1024 - 1024 - fixed) / (16 * QC + 8 * NEUR));
+  const long long fixed = (long long)2 * 8 * kPS * 16 + (long long)2 * 8 * kGS * 16;
+  int ns_cap = (int)((227LL * 1024 - 1024 - fixed) / (16 * QC + 12 * NEUR));
+  if (ns_cap > kMaxTailSamples) ns_cap = kMaxTailSamples;
   int top = 0;  // largest instantiated count within the cap
   for (int i = 0; i < kNn; ++i)
     if (kNspt[i] * SGF <= ns_cap) top = i;
@@ -472,8 +534,8 @@ void plan_stream(RecPlan& p, int B, int H, int num_sms) {
   p.threads_fwd = p.threads_bwd = kNT;
   p.slots_bwd = ngroups;
   p.smem_fwd = (size_t)2 * kPC * NEUR * 16 + (size_t)2 * ns * kPC * 4;
-  p.smem_bwd = (size_t)2 * NEUR * QC * 16 + (size_t)2 * 4 * NEUR * QC * 4 + (size_t)4 * ns * QC * 4 +
-               (size_t)2 * ns * NEUR * 4;
+  p.smem_bwd = (size_t)fixed + (size_t)4 * ns * QC * 4 +
+               (size_t)3 * ns * NEUR * 4;
   p.scratch_fwd = (size_t)2 * B * HP;
   p.scratch_bwd = (size_t)7 * B * HP;
 }
