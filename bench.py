@@ -382,6 +382,11 @@ def main():
     per_launch_s = tot_ms / max(1, n_l) / 1e3
     achieved = visits[dom] / per_launch_s / 1e9
     peak = sms * 16 / 2 * f_mhz * 1e6 / 1e9  # Gvisits/s: 16 MUFU/clk/SM, 2 MUFU per visit
+    # the kernels' own bound: tanh-form gates issue 1 MUFU op per visit; the
+    # forward kernels then need 3 FP32 lane-ops per visit (MUFU-bound, 16
+    # visits/clk/SM), the backward ones 10 (FP32-pipe-bound, 128/10 per clk/SM)
+    own_rate = {"recurrent_fwd": 16.0, "sensory_fwd": 16.0, "recurrent_bwd": 12.8, "sensory_bwd": 12.8}
+    peak_own = sms * own_rate[dom] * f_mhz * 1e6 / 1e9
     kernels = {k: {"ms_total": round(v[0], 3), "launches": v[1], "share": round(v[0] / max(1e-9, sum(
         t for t, _ in ktimes.values())), 4)} for k, v in ktimes.items()}
     # whole-step ceiling with the survey's counting convention (4 MUFU per fwd+bwd synapse visit)
@@ -412,6 +417,9 @@ def main():
                      "traffic_unit": "bytes per launch (ncu capture, scaled)",
                      "peak_basis": f"{sms} SMs x 16 MUFU/clk / 2 MUFU per visit at sm_max {f_mhz:.0f} MHz ({peaks_kind})",
                      "step_frac_survey_convention": t_roof / (ms / 1e3),
+                     "frac_own_bound": achieved / peak_own,
+                     "own_bound_basis": ("1 MUFU + 10 FP32 lane-ops per visit (FP32-bound, 12.8 visits/clk/SM)"
+                                         if own_rate[dom] < 16 else "1 MUFU per visit (16 visits/clk/SM)"),
                      "recurrent_frac_survey_convention": rec_frac,
                      "sensory_fwd_hbm_gbs": sens_gbs,
                      "sensory_fwd_hbm_frac": sens_gbs / float(peaks.get("hbm_gbs", 6650.0))},

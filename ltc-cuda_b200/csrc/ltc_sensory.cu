@@ -182,9 +182,13 @@ struct SensBwdGeom {
 // q0 + sub(j, g).  The per-row adjoint loads (8 columns of gsn, gsd) are shared
 // by the two inputs.
 // TS (tanh space): the recurrent backward also produced the column sums of g_sn,
-// g_sd (= sum of a_n, a_d); the gate is evaluated as tn = tanh(-z/2) = -t, the
-// staged adjoints are scaled to a' = -g/4, and the finish kernel adds the g/2 part
-// of sum g*act:  dL/dz = (a'_n swe + a'_d sw)(tn^2 - 1),  g act = g/2 + 2 a' tn.
+// g_sd (= sum of a_n, a_d); the gate is evaluated as tn = tanh(-z/2) = -t, with
+// a' = -g/4 the finish kernel adds the g/2 part of sum g*act:
+//   dL/dz = (a'_n swe + a'_d sw)(tn^2 - 1),  g act = g/2 + 2 a' tn.
+// The -1/4 is folded into the weight registers (dz) and into the final scale of
+// the An/Ad sums, so the adjoint tiles are staged raw.
+// Tiles of kRT rows (gsn, gsd, x) are double-buffered with cp.async (zero-filled
+// outside the valid rows/columns), so the next tile's loads overlap this one's math.
 template <int QC, bool TS>
 __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc, long long rows_per_split,
                                                           float* dxpart) {
@@ -193,9 +197,8 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
   constexpr int NI = 2 * kSB;
   using LR = LaneReduce<TPC, NI>;
   extern __shared__ __align__(16) float smem[];
-  float* GN = smem;               // [kRT][LDG]
-  float* GD = GN + kRT * LDG;     // [kRT][LDG]
-  float* XS = GD + kRT * LDG;     // [kRT][DPC]
+  constexpr int TILE = 2 * kRT * LDG + kRT * DPC;  // floats of one buffer
+  // buffer b: GN [kRT][LDG], GD [kRT][LDG], XS [kRT][DPC] at smem + b*TILE
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int c = tid / TPC, g = tid % TPC;
@@ -212,7 +215,8 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
       const int d = d0 + c + r * NGD;
       float4 pk = make_float4(0.f, 0.f, 0.f, 0.f);
       if (d < D) pk = a.spack[(long long)d * HP + q0 + G::sub(j, g)];
-      sl[r][j] = TS ? -pk.x : pk.x; nm[r][j] = TS ? -pk.y : pk.y; sw[r][j] = pk.z; swe[r][j] = pk.w;
+      sl[r][j] = TS ? -pk.x : pk.x; nm[r][j] = TS ? -pk.y : pk.y;
+      sw[r][j] = TS ? -0.25f * pk.z : pk.z; swe[r][j] = TS ? -0.25f * pk.w : pk.w;
       An[r][j] = Ad[r][j] = Dz[r][j] = Dzx[r][j] = 0.f;
     }
   const int own = LR::own_base(lane);
@@ -222,22 +226,35 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
   const long long r_end = min(a.rows, r_begin + rows_per_split);
   const long long ndx = a.rows * D;
 
-  for (long long rt = r_begin; rt < r_end; rt += kRT) {
+  auto stage = [&](long long rt, int buf) {
     const int nr = (int)min((long long)kRT, r_end - rt);
-    __syncthreads();
+    float* GN = smem + buf * TILE;
+    float* GD = GN + kRT * LDG;
+    float* XS = GD + kRT * LDG;
     for (int i = tid; i < kRT * QC; i += NT) {
       const int r = i / QC, cc = i % QC;
       const bool ok = r < nr && cc < hq;
-      const long long src = (rt + r) * H + q0 + cc;
-      const float sc = TS ? -0.25f : 1.0f;
-      GN[r * LDG + cc] = ok ? sc * a.gsn[src] : 0.f;
-      GD[r * LDG + cc] = ok ? sc * a.gsd[src] : 0.f;
+      const long long src = ok ? (rt + r) * H + q0 + cc : 0;
+      cp_async4_zfill(GN + r * LDG + cc, a.gsn + src, ok);
+      cp_async4_zfill(GD + r * LDG + cc, a.gsd + src, ok);
     }
     for (int i = tid; i < kRT * DPC; i += NT) {
       const int r = i / DPC, cc = i % DPC;
-      XS[i] = (r < nr && d0 + cc < D) ? a.x[(rt + r) * D + d0 + cc] : 0.f;
+      const bool ok = r < nr && d0 + cc < D;
+      cp_async4_zfill(XS + i, a.x + (ok ? (rt + r) * D + d0 + cc : 0), ok);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  if (r_begin < r_end) stage(r_begin, 0);
+  int buf = 0;
+  for (long long rt = r_begin; rt < r_end; rt += kRT, buf ^= 1) {
+    const int nr = (int)min((long long)kRT, r_end - rt);
+    cp_async_wait_all();
+    __syncthreads();  // tile rt landed; the other buffer is free again
+    if (rt + kRT < r_end) stage(rt + kRT, buf ^ 1);
+    const float* GN = smem + buf * TILE;
+    const float* GD = GN + kRT * LDG;
+    const float* XS = GD + kRT * LDG;
     const int nblk = (nr + kSB - 1) / kSB;
     for (int blk = 0; blk < nblk; ++blk) {
       float acc[1][NI];
@@ -316,11 +333,12 @@ __global__ void __launch_bounds__(256, 1) sens_bwd_kernel(SensBwdArgs a, int nqc
     const int d = d0 + c + r * NGD;
     if (d >= D) continue;
     float* part = a.part + (long long)blockIdx.y * 4 * slab + (long long)d * HP + q0;
+    const float sc = TS ? -0.25f : 1.0f;  // An/Ad were summed with the raw adjoints
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int cc = G::sub(j, g);
-      part[cc] = An[r][j];
-      part[slab + cc] = Ad[r][j];
+      part[cc] = sc * An[r][j];
+      part[slab + cc] = sc * Ad[r][j];
       part[2 * slab + cc] = Dz[r][j];
       part[3 * slab + cc] = Dzx[r][j];
     }
@@ -389,7 +407,7 @@ cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float
   long long rps = (a.rows + p.nsplit - 1) / p.nsplit;
   rps = (rps + kRT - 1) / kRT * kRT;
   dim3 grid(p.ndc * p.nqc, p.nsplit);
-  const size_t smem = (size_t)2 * kRT * (p.qc + 4) * 4 + (size_t)kRT * p.dpc * 4;
+  const size_t smem = 2 * ((size_t)2 * kRT * (p.qc + 4) * 4 + (size_t)kRT * p.dpc * 4);  // double-buffered
   cudaError_t e;
 #define LTC_SB_CASE(QCV)                                                                                 \
   case QCV:                                                                                              \
