@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the configuration's global batch (profiling captures of smaller cases)")
     ap.add_argument("--seq", type=int, default=None, help="override the sequence length T (profiling captures)")
+    ap.add_argument("--lean", type=int, default=0,
+                    help="1: memory-lean training (step-boundary states saved, unfolds recomputed in the backward)")
     ap.add_argument("--graph", type=int, default=None,
                     help="1 (default): replay the whole step as a captured CUDA graph; 0: eager launches")
     return ap.parse_args()
@@ -208,6 +210,7 @@ def main():
         return
 
     import ltc_cuda
+    ltc_cuda.set_lean_save(bool(args.lean))
     import ltc_layer
     from data_parallel import FlatGradBucket, shard_range, training_step
 
@@ -408,7 +411,8 @@ def main():
                    "step": "train (fwd+bwd+allreduce+adam)" if cfg.training_step else "fwd+bwd",
                    "parallelism": f"dp{world}", "per_rank_batch": Bl,
                    "l2": "256 MB flush write between steps (inside the timed region)",
-                   "cuda_graph": use_graph if graph_note is None else graph_note},
+                   "cuda_graph": use_graph if graph_note is None else graph_note,
+                   "saved_state": "step boundaries, unfolds recomputed (lean)" if args.lean else "every unfold"},
         "e2e": e2e,
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
                      "frac": achieved / peak,

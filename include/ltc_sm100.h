@@ -36,6 +36,16 @@ typedef struct {
 } LtcDims;
 
 #define LTC_FLAG_FORCE_WIDE 1 /* use the streamed wide-H kernels even for H <= 64 */
+/* Memory-lean training (the reference keeps every unfold's state: v_buffers
+ * (T,U,B,H), csrc/ltc_kernels.cu:1205-1212).  The forward saves only the state
+ * at each step boundary ((T+1)*B*H floats instead of (2*T*U+1)*B*H); the
+ * backward recomputes the unfolds segment by segment (lean_chunk_steps steps per
+ * segment, newest first) with the forward kernels and accumulates the parameter
+ * partials across segments.  Cost: one extra recurrent + sensory forward. */
+#define LTC_FLAG_LEAN_SAVE 2
+/* Bits 8..23 of flags, if nonzero, fix the lean segment length in steps
+ * (otherwise it is sized for about 512 MiB of per-unfold state). */
+#define LTC_LEAN_CHUNK_SHIFT 8
 
 /* The 11 parameter inputs of ltc_full_forward (csrc/ltc_kernels.cu:1167-1178),
  * untransposed, in the same order. */
@@ -81,6 +91,7 @@ typedef struct {
   int32_t wide;       /* 1 if the wide-H kernels will run */
   int32_t padded_h;   /* neuron count the kernels pad H to */
   int32_t fwd_ctas, bwd_ctas;
+  int32_t lean_chunk_steps; /* steps per recomputed segment (LTC_FLAG_LEAN_SAVE), else 0 */
 } LtcPlan;
 
 int ltc_plan(const LtcDims* dims, LtcPlan* out);

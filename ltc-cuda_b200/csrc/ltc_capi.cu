@@ -125,6 +125,8 @@ struct Layout {
   SensBwdPlan sp;
   long long rows;
   size_t saved_floats_v, saved_floats_r;
+  bool lean;  // LTC_FLAG_LEAN_SAVE: saved = step-boundary states; the backward recomputes segments
+  int tc;     // lean segment length in steps
 };
 
 int check_dims(const LtcDims* d) {
@@ -148,8 +150,26 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
   L->rows = (long long)d->B * d->T;
   L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
   const size_t tu = (size_t)d->T * d->ode_unfolds;
-  L->saved_floats_v = (tu + 1) * d->B * d->H;
-  L->saved_floats_r = tu * d->B * d->H;
+  L->lean = (d->flags & LTC_FLAG_LEAN_SAVE) != 0;
+  L->tc = 0;
+  if (L->lean) {
+    // saved: h0 (B,H) + the step outputs (B,T,H), i.e. the state at every step boundary
+    L->saved_floats_v = (size_t)(d->T + 1) * d->B * d->H;
+    L->saved_floats_r = 0;
+    const int fixed = (d->flags >> LTC_LEAN_CHUNK_SHIFT) & 0xFFFF;
+    if (fixed > 0) {
+      L->tc = fixed;
+    } else {  // about 512 MiB of per-segment state (V, R, staged x and sensory sums)
+      const double per_step =
+          4.0 * ((2.0 * d->ode_unfolds + 4.0) * d->B * d->H + (double)d->B * d->D);
+      const double n = (512.0 * 1024 * 1024) / per_step;
+      L->tc = n < 1.0 ? 1 : (n > d->T ? d->T : (int)n);
+    }
+    if (L->tc > d->T) L->tc = d->T;
+  } else {
+    L->saved_floats_v = (tu + 1) * d->B * d->H;
+    L->saved_floats_r = tu * d->B * d->H;
+  }
   return 0;
 }
 
@@ -172,6 +192,8 @@ size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
 struct BwdBuffers {
   float4 *pack, *packT, *spack, *nrn;
   float *gsn, *gsd, *rpart, *rpartn, *spart, *dxpart, *scratch;
+  // lean backward: one segment's staged inputs, recomputed state and outputs
+  float *xc, *snc, *sdc, *gsnc, *gsdc, *Vc, *Rc, *hs, *ghA, *ghB, *fscratch;
 };
 size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   Carver c(ws);
@@ -187,6 +209,21 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->spart = c.take<float>(L.sp.part_floats);
   b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
   b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
+  b->xc = b->snc = b->sdc = b->gsnc = b->gsdc = b->Vc = b->Rc = b->hs = b->ghA = b->ghB = b->fscratch = nullptr;
+  if (L.lean) {
+    const size_t BH = (size_t)d->B * d->H, tcu = (size_t)L.tc * d->ode_unfolds;
+    b->xc = c.take<float>((size_t)d->B * L.tc * d->D);
+    b->snc = c.take<float>(BH * L.tc);
+    b->sdc = c.take<float>(BH * L.tc);
+    b->gsnc = c.take<float>(BH * L.tc);
+    b->gsdc = c.take<float>(BH * L.tc);
+    b->Vc = c.take<float>((tcu + 1) * BH);
+    b->Rc = c.take<float>(tcu * BH);
+    b->hs = c.take<float>(BH);
+    b->ghA = c.take<float>(BH);
+    b->ghB = c.take<float>(BH);
+    b->fscratch = L.rp.scratch_fwd ? c.take<float>(L.rp.scratch_fwd) : nullptr;
+  }
   return c.off + 256;
 }
 
@@ -207,6 +244,9 @@ int check_params(const LtcParams* p) {
     if (!q) return fail("a parameter pointer is NULL");
   return 0;
 }
+
+int lean_recurrent_backward(const LtcDims* dims, const Layout& L, const DeviceInfo& di, const BwdBuffers& b,
+                            const float* ck, const float* x, RecBwdArgs ra, cudaStream_t st);
 
 }  // namespace
 
@@ -333,6 +373,7 @@ int ltc_plan(const LtcDims* dims, LtcPlan* out) {
   out->padded_h = L.rp.HP;
   out->fwd_ctas = L.rp.grid_fwd;
   out->bwd_ctas = L.rp.grid_bwd;
+  out->lean_chunk_steps = L.lean ? L.tc : 0;
   g_last_error.clear();
   return 0;
 }
@@ -373,7 +414,7 @@ int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, co
   RecFwdArgs ra{};
   ra.pack = b.pack; ra.nrn = b.nrn; ra.sn = b.sn; ra.sd = b.sd; ra.h0 = h0;
   ra.out = outputs; ra.hT = h_final;
-  if (saved) {
+  if (saved && !L.lean) {
     Carver c(saved);
     ra.V = c.take<float>(L.saved_floats_v);
     ra.R = c.take<float>(L.saved_floats_r);
@@ -385,6 +426,15 @@ int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, co
     e = launch_recurrent_fwd(ra, L.rp, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "recurrent_fwd");
+  if (saved && L.lean) {  // step-boundary states: h0, then the outputs
+    Carver c(saved);
+    float* ck = c.take<float>(L.saved_floats_v);
+    const size_t bh = (size_t)dims->B * dims->H * sizeof(float);
+    e = h0 ? cudaMemcpyAsync(ck, h0, bh, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(ck, 0, bh, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(ck + (size_t)dims->B * dims->H, outputs, bh * dims->T, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "lean checkpoint copy");
+  }
   g_last_error.clear();
   return 0;
 }
@@ -423,18 +473,22 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   Carver sc(const_cast<void*>(saved));
   RecBwdArgs ra{};
   ra.pack = b.pack; ra.packT = b.packT; ra.nrn = b.nrn;
-  ra.V = sc.take<float>(L.saved_floats_v);
-  ra.R = sc.take<float>(L.saved_floats_r);
   ra.gout = grad_outputs; ra.go_sb = go_strides[0]; ra.go_st = go_strides[1]; ra.go_sh = go_strides[2];
   ra.gstate = grad_state; ra.gsn = b.gsn; ra.gsd = b.gsd; ra.gh0 = grads->state;
   ra.part = b.rpart; ra.partn = b.rpartn;
   ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
   ra.ns = L.rp.ns_bwd; ra.scratch = b.scratch;
-  {
-    TimedLaunch tl(LTC_KERNEL_RECURRENT_BWD, st);
-    e = launch_recurrent_bwd(ra, L.rp, st);
+  if (!L.lean) {
+    ra.V = sc.take<float>(L.saved_floats_v);
+    ra.R = sc.take<float>(L.saved_floats_r);
+    {
+      TimedLaunch tl(LTC_KERNEL_RECURRENT_BWD, st);
+      e = launch_recurrent_bwd(ra, L.rp, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "recurrent_bwd");
+  } else if (int rc = lean_recurrent_backward(dims, L, di, b, sc.take<float>(L.saved_floats_v), x, ra, st)) {
+    return rc;
   }
-  if (e != cudaSuccess) return cuda_fail(e, "recurrent_bwd");
 
   SensBwdArgs sa{};
   sa.spack = b.spack; sa.x = x; sa.gsn = b.gsn; sa.gsd = b.gsd; sa.dx = grads->x_seq;
@@ -465,6 +519,78 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
 }
 
 }  // extern "C"
+
+namespace {
+// Lean backward of the recurrent part: segments of L.tc steps, newest first.  For
+// each: stage its x rows and start state, recompute its sensory sums and unfolds
+// (V, R) with the forward kernels, run the recurrent backward over it (adjoint in
+// from the newer segment, parameter partials accumulated), and scatter its g_sn,
+// g_sd rows into the full buffers the sensory backward reads.
+int lean_recurrent_backward(const LtcDims* dims, const Layout& L, const DeviceInfo& di, const BwdBuffers& b,
+                            const float* ck, const float* x, RecBwdArgs ra, cudaStream_t st) {
+  const int B = dims->B, T = dims->T, D = dims->D, H = dims->H, HP = L.rp.HP;
+  const size_t f4 = sizeof(float);
+  const float* gin = ra.gstate;  // dL/d(state at the segment's end)
+  float* gbuf[2] = {b.ghA, b.ghB};
+  int gsel = 0;
+  cudaError_t e = cudaSuccess;
+  const int nseg = (T + L.tc - 1) / L.tc;
+  for (int seg = nseg - 1; seg >= 0; --seg) {
+    const int t0 = seg * L.tc, tc = T - t0 < L.tc ? T - t0 : L.tc;
+    // x rows (b, t0 .. t0+tc) -> (B*tc, D); the state at t0 -> (B, H)
+    e = cudaMemcpy2DAsync(b.xc, (size_t)tc * D * f4, x + (size_t)t0 * D, (size_t)T * D * f4, (size_t)tc * D * f4,
+                          B, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "lean: stage x");
+    const float* h_start = ck;  // h0 block
+    if (t0 > 0) {
+      e = cudaMemcpy2DAsync(b.hs, (size_t)H * f4, ck + (size_t)B * H + (size_t)(t0 - 1) * H, (size_t)T * H * f4,
+                            (size_t)H * f4, B, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "lean: stage state");
+      h_start = b.hs;
+    }
+    SensFwdArgs sa{};
+    sa.spack = b.spack; sa.x = b.xc; sa.sn = b.snc; sa.sd = b.sdc; sa.rows = (long long)B * tc;
+    sa.D = D; sa.H = H; sa.HP = HP;
+    {
+      TimedLaunch tl(LTC_KERNEL_SENSORY_FWD, st);
+      e = launch_sensory_fwd(sa, di.sms, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "lean: sensory_fwd");
+    RecFwdArgs fa{};
+    fa.pack = b.pack; fa.nrn = b.nrn; fa.sn = b.snc; fa.sd = b.sdc; fa.h0 = h_start;
+    fa.out = nullptr; fa.hT = nullptr; fa.V = b.Vc; fa.R = b.Rc;
+    fa.B = B; fa.T = tc; fa.H = H; fa.U = dims->ode_unfolds; fa.HP = HP;
+    fa.ns = L.rp.ns_fwd; fa.eps = dims->epsilon; fa.scratch = b.fscratch;
+    {
+      TimedLaunch tl(LTC_KERNEL_RECURRENT_FWD, st);
+      e = launch_recurrent_fwd(fa, L.rp, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "lean: recurrent_fwd");
+    RecBwdArgs sb = ra;
+    sb.V = b.Vc; sb.R = b.Rc; sb.T = tc;
+    sb.gout = ra.gout + (long long)t0 * ra.go_st;
+    sb.gstate = gin;
+    sb.gsn = b.gsnc; sb.gsd = b.gsdc;
+    sb.gh0 = t0 == 0 ? ra.gh0 : gbuf[gsel];
+    sb.accumulate = seg != nseg - 1;
+    {
+      TimedLaunch tl(LTC_KERNEL_RECURRENT_BWD, st);
+      e = launch_recurrent_bwd(sb, L.rp, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "lean: recurrent_bwd");
+    float* gfull[2] = {ra.gsn, ra.gsd};
+    const float* gseg[2] = {b.gsnc, b.gsdc};
+    for (int k = 0; k < 2; ++k) {
+      e = cudaMemcpy2DAsync(gfull[k] + (size_t)t0 * H, (size_t)T * H * f4, gseg[k], (size_t)tc * H * f4,
+                            (size_t)tc * H * f4, B, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "lean: scatter g_sn/g_sd");
+    }
+    gin = sb.gh0;
+    gsel ^= 1;
+  }
+  return 0;
+}
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // Step-level calls: the reference's per-step exports (csrc/ltc_kernels.cu:675-950),

@@ -87,8 +87,8 @@ struct RecFwdArgs {
   const float* sn;      // (B*T, H)
   const float* sd;      // (B*T, H)
   const float* h0;      // (B,H) or null (zeros)
-  float* out;           // (B,T,H)
-  float* hT;            // (B,H)
+  float* out;           // (B,T,H) or null (recomputation for a lean backward)
+  float* hT;            // (B,H) or null
   float* V;             // (T*U+1, B, H) or null
   float* R;             // (T*U, B, H) or null
   int B, T, H, U, HP;
@@ -113,6 +113,7 @@ struct RecBwdArgs {
   int B, T, H, U, HP;
   int ns;
   float* scratch;       // plan.scratch_bwd floats (streamed path)
+  int accumulate;       // add to part/partn (segments of a lean backward) instead of overwriting
 };
 struct RecPlan {
   bool wide;       // not the register-resident kernels (streamed or generic wide-H)

@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
             a.V[(n * B + bs) * H + q] = v;
             a.R[(n * B + bs) * H + q] = rr;
           }
-          if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
+          if (u == U - 1 && a.out) a.out[(bs * T + t) * H + q] = vnew;
         }
       }
       if constexpr (CL > 1) {
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
     const int s = i / G::NEUR, h = nb + i % G::NEUR;
     if (h >= H) continue;
     const long long bs = b0 + s;
-    a.hT[bs * H + h] = vc[s * LDV + h];
+    if (a.hT) a.hT[bs * H + h] = vc[s * LDV + h];
     if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[s * LDV + h];
   }
   if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may address it
@@ -554,10 +554,19 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       const int idx = (c + r * NG) * HP + G::sub(j, g);
       const int k = j / 2;
       const bool hi = j & 1;
-      part[idx] = hi ? Gwe[r][k].y : Gwe[r][k].x;
-      part[HP * HP + idx] = hi ? Gwp[r][k].y : Gwp[r][k].x;
-      part[2 * HP * HP + idx] = hi ? Gdz[r][k].y : Gdz[r][k].x;
-      part[3 * HP * HP + idx] = hi ? Gdzv[r][k].y : Gdzv[r][k].x;
+      const float v0 = hi ? Gwe[r][k].y : Gwe[r][k].x, v1 = hi ? Gwp[r][k].y : Gwp[r][k].x;
+      const float v2 = hi ? Gdz[r][k].y : Gdz[r][k].x, v3 = hi ? Gdzv[r][k].y : Gdzv[r][k].x;
+      if (a.accumulate) {
+        part[idx] += v0;
+        part[HP * HP + idx] += v1;
+        part[2 * HP * HP + idx] += v2;
+        part[3 * HP * HP + idx] += v3;
+      } else {
+        part[idx] = v0;
+        part[HP * HP + idx] = v1;
+        part[2 * HP * HP + idx] = v2;
+        part[3 * HP * HP + idx] = v3;
+      }
     }
   // per-neuron sums: each lane holds the partial of its own row; fixed-order sum
   // over the lanes of the group through shared memory.
@@ -578,7 +587,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     for (int k = 0; k < 5; ++k) {
       float sum = 0.f;
       for (int l = 0; l < TPC; ++l) sum += red[(k * HP + row) * TPC + l];
-      pn[k * HP + row] = sum;
+      pn[k * HP + row] = a.accumulate ? pn[k * HP + row] + sum : sum;
     }
   }
   if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may address it

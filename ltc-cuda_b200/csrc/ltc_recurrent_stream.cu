@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
             a.V[(n * B + bs) * H + q] = v;
             a.R[(n * B + bs) * H + q] = r;
           }
-          if (u == U - 1) a.out[row * H + q] = vnew;
+          if (u == U - 1 && a.out) a.out[row * H + q] = vnew;
         }
       }
       cluster.sync();  // release this unfold's states / acquire the peers'
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
     const int s = i / NEUR, h = nb + i % NEUR;
     if (h >= H) continue;
     const long long bs = b0 + s;
-    a.hT[bs * H + h] = vc[bs * HP + h];
+    if (a.hT) a.hT[bs * H + h] = vc[bs * HP + h];
     if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[bs * HP + h];
   }
 }
@@ -232,8 +232,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   };
   stage_vp(NTU - 1);
   cp_async_commit();
-  // zero this CTA's rows of the gradient slab
-  for (int i = tid; i < NEUR * HP; i += kNT) {
+  // zero this CTA's rows of the gradient slab (kept when accumulating segments)
+  for (int i = tid; i < (a.accumulate ? 0 : NEUR * HP); i += kNT) {
     const long long o = (long long)(nb + i / HP) * HP + i % HP;
     slab[o] = 0.f;
     slab[hp2 + o] = 0.f;
@@ -461,9 +461,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   }
   if (ql == 0) {
     float* pn = a.partn + (long long)grp * 3 * HP;
-    pn[p] = gcm;
-    pn[HP + p] = ggl;
-    pn[2 * HP + p] = gvl;
+    pn[p] = a.accumulate ? pn[p] + gcm : gcm;
+    pn[HP + p] = a.accumulate ? pn[HP + p] + ggl : ggl;
+    pn[2 * HP + p] = a.accumulate ? pn[2 * HP + p] + gvl : gvl;
   }
 }
 

@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(512, 1) rec_fwd_wide(RecFwdArgs a) {
             a.V[(n * B + bs) * H + q] = v;
             a.R[(n * B + bs) * H + q] = r;
           }
-          if (u == U - 1) a.out[(bs * T + t) * H + q] = vnew;
+          if (u == U - 1 && a.out) a.out[(bs * T + t) * H + q] = vnew;
         }
       }
       cur ^= 1;
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(512, 1) rec_fwd_wide(RecFwdArgs a) {
   for (int i = tid; i < nvalid * H; i += blockDim.x) {
     const int s = i / H, h = i % H;
     const long long bs = b0 + s;
-    a.hT[bs * H + h] = vc[s * HPW + h];
+    if (a.hT) a.hT[bs * H + h] = vc[s * HPW + h];
     if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[s * HPW + h];
   }
 }
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(512, 1) rec_bwd_wide(RecBwdArgs a) {
   const bool pvalid = p < H;
 
   for (int i = tid; i < 4 * ns * HPW; i += blockDim.x) AN[i] = 0.f;
-  for (int q = 0; q < HPW; ++q) {
+  for (int q = 0; q < (a.accumulate ? 0 : HPW); ++q) {  // kept when accumulating segments
     slab[q * HPW] = 0.f;
     slab[hp2 + q * HPW] = 0.f;
     slab[2 * hp2 + q * HPW] = 0.f;
@@ -264,9 +264,9 @@ __global__ void __launch_bounds__(512, 1) rec_bwd_wide(RecBwdArgs a) {
   }
   cp_async_wait_all();
   float* pn = a.partn + ((long long)blockIdx.x * SG + sg) * 3 * HPW;
-  pn[p] = gcm;
-  pn[HPW + p] = ggl;
-  pn[2 * HPW + p] = gvl;
+  pn[p] = a.accumulate ? pn[p] + gcm : gcm;
+  pn[HPW + p] = a.accumulate ? pn[HPW + p] + ggl : ggl;
+  pn[2 * HPW + p] = a.accumulate ? pn[2 * HPW + p] + gvl : gvl;
 }
 
 template <int NSPT>

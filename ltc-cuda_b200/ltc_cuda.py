@@ -39,6 +39,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("LTC_SM100_LIB", os.path.join(_HERE, "libltc_sm100.so"))
 
 LTC_FLAG_FORCE_WIDE = 1
+LTC_FLAG_LEAN_SAVE = 2
+LTC_LEAN_CHUNK_SHIFT = 8
 
 
 class LtcDims(ctypes.Structure):
@@ -61,7 +63,8 @@ class LtcGrads(ctypes.Structure):
 class LtcPlan(ctypes.Structure):
     _fields_ = [("saved_bytes", ctypes.c_size_t), ("fwd_workspace_bytes", ctypes.c_size_t),
                 ("bwd_workspace_bytes", ctypes.c_size_t), ("wide", ctypes.c_int32),
-                ("padded_h", ctypes.c_int32), ("fwd_ctas", ctypes.c_int32), ("bwd_ctas", ctypes.c_int32)]
+                ("padded_h", ctypes.c_int32), ("fwd_ctas", ctypes.c_int32), ("bwd_ctas", ctypes.c_int32),
+                ("lean_chunk_steps", ctypes.c_int32)]
 
 
 # Exported symbols and their C signatures (include/ltc_sm100.h).
@@ -168,7 +171,18 @@ _flags = 0
 def set_force_wide(on: bool) -> None:
     """Route every call through the streamed wide-H kernels (testing the second path)."""
     global _flags
-    _flags = LTC_FLAG_FORCE_WIDE if on else 0
+    _flags = (_flags | LTC_FLAG_FORCE_WIDE) if on else (_flags & ~LTC_FLAG_FORCE_WIDE)
+
+
+def set_lean_save(on: bool, chunk_steps: int = 0) -> None:
+    """Memory-lean training: the forward keeps only the state at each step boundary
+    and the backward recomputes the unfolds segment by segment (``chunk_steps`` steps
+    per segment; 0 = sized by the library).  Applies to forwards run afterwards; a
+    forward's own mode is remembered for its backward."""
+    global _flags
+    _flags &= ~(LTC_FLAG_LEAN_SAVE | (0xFFFF << LTC_LEAN_CHUNK_SHIFT))
+    if on:
+        _flags |= LTC_FLAG_LEAN_SAVE | ((int(chunk_steps) & 0xFFFF) << LTC_LEAN_CHUNK_SHIFT)
 
 
 KERNEL_NAMES = ("pack_fwd", "sensory_fwd", "recurrent_fwd", "pack_bwd", "recurrent_bwd", "sensory_bwd",
@@ -239,6 +253,8 @@ class _CudaModule:
             _check(lib.ltc_forward(ctypes.byref(dims), ctypes.byref(_params_struct(params)), x.data_ptr(),
                                    h0.data_ptr(), outputs.data_ptr(), h_final.data_ptr(), _ptr(saved),
                                    ws.data_ptr(), pl.fwd_workspace_bytes, stream), "ltc_full_forward")
+        if saved is not None:
+            saved._ltc_flags = dims.flags  # the backward must read it with the same layout
         return [outputs, h_final, saved] if save_intermediates else [outputs, h_final]
 
     @staticmethod
@@ -262,7 +278,7 @@ class _CudaModule:
             gs = _as_f32(grad_final_state, dev, "grad_final_state")
         grads = [torch.empty(B, T, D, device=dev), torch.empty(B, H, device=dev)] + \
                 [torch.empty_like(p) for p in params]
-        dims = make_dims(B, T, D, H, ode_unfolds, epsilon, _flags)
+        dims = make_dims(B, T, D, H, ode_unfolds, epsilon, getattr(saved, "_ltc_flags", _flags))
         strides = (ctypes.c_int64 * 3)(*grad_outputs.stride())
         with torch.cuda.device(dev):
             pl = plan(dims)
