@@ -33,9 +33,10 @@ import torch.distributed as dist  # noqa: E402
 import synth  # noqa: E402
 
 # DRAM bytes per (sample, timestep) of a kernel from one ncu capture of a smaller case
-# of the same configuration (profiles/rec_bwd_fast_c3_b1184.md), scaled to a launch
-# by the (b,t) units it processes.
-NCU_TRAFFIC_PER_BT = {("c3", "recurrent_bwd"): 3535.0}
+# of the same configuration (c3 shape at B=1184: dram__bytes_read + dram__bytes_write
+# = 466.5 + 70.4 MB over 1184*128 (b,t)), scaled to a launch by the (b,t) units it
+# processes (the traffic is the saved V/R read and the g_sn/g_sd write, linear in B).
+NCU_TRAFFIC_PER_BT = {("c3", "recurrent_bwd"): 3543.0}
 
 METRIC = "fwd+bwd sequence-timesteps/sec (B·T/s) at 1/2/4/8 B200; % FP32 roofline"
 UNIT = "B*T/s"
