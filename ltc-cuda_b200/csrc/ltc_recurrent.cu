@@ -64,6 +64,7 @@ struct Geometry {
   __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (HP / 2) + 4 * g + (j % 4); }
 };
 
+#if !LTC_FWD_TANH
 // Gate of synapse j in the forward kernels: synapses j < kMufuRcp use the MUFU
 // reciprocal, the rest the FMA-pipe Newton reciprocal, balancing the two pipes.
 constexpr int kMufuRcp = LTC_FWD_MUFU_RCP;
@@ -71,6 +72,7 @@ constexpr int kMufuRcp = LTC_FWD_MUFU_RCP;
 __device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
   return j < kMufuRcp ? gate(sl, nm, v) : gate_newton(sl, nm, v);
 }
+#endif
 
 // Cluster helpers: with CL > 1 the CTAs of a cluster share one sample group and
 // each owns HP/CL neurons; per-neuron results of an unfold are sent to every
