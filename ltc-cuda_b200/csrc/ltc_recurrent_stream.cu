@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   const float4 np_ = a.nrn[p];
   const float cm = np_.x, gl = np_.y, vl = np_.z;
   const bool pvalid = p < H;
-  float gcm = 0.f, ggl = 0.f, gvl = 0.f;
+  float gcm = 0.f, ggl = 0.f, gvl = 0.f, san = 0.f, sad = 0.f;
 
   // adjoint rows of padded samples in the last register block must read as 0
   const int nblk = (nvalid + kSB - 1) / kSB;
@@ -252,12 +252,15 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
     gcm = fmaf(an, vin - vout, gcm);
     ggl = fmaf(an, vl - vout, ggl);
     gvl = fmaf(an, gl, gvl);
+    san += an;
+    sad += ad;
     const long long o = bs * HP + p;
     GSNg[o] = first ? an : GSNg[o] + an;
     GSDg[o] = first ? ad : GSDg[o] + ad;
     DIRg[o] = an * cm;
-    ANg[(m & 1) * SB_ + o] = an;
-    ADg[(m & 1) * SB_ + o] = ad;
+    // the synapse pass works in tanh space: it reads a' = -a/4
+    ANg[(m & 1) * SB_ + o] = -0.25f * an;
+    ADg[(m & 1) * SB_ + o] = -0.25f * ad;
   };
 
   // initial prep of unfold NTU-1: g = dL/dout[:, T-1] + dL/dstate; padded rows write zeros
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
 
   const int own = LR::own_base(lane);
   const bool writer = LR::writer(lane);
-  const float2 half2 = make_float2(0.5f, 0.5f), nhalf2 = make_float2(-0.5f, -0.5f);
+  const float2 m1 = make_float2(-1.f, -1.f);
   int t = T - 1, k = U - 1;
   for (int n = NTU - 1; n >= 0; --n) {
     for (int i = tid; i < ns * NEUR; i += kNT) DV[i] = 0.f;
@@ -326,8 +329,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const float4 p0 = pk[(2 * kk) * kPS], p1 = pk[(2 * kk + 1) * kPS];
-        sl2[kk] = make_float2(p0.x, p1.x);
-        nm2[kk] = make_float2(p0.y, p1.y);
+        // negated half-scale constants: the gate argument is -z/2, so tanh gives -t
+        sl2[kk] = make_float2(-p0.x, -p1.x);
+        nm2[kk] = make_float2(-p0.y, -p1.y);
         wp2[kk] = make_float2(p0.z, p1.z);
         we2[kk] = make_float2(p0.w, p1.w);
       }
@@ -362,12 +366,13 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
           float2 dv = make_float2(0.f, 0.f);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const float2 th = tanh2(fma2(sl2[kk], vp2, nm2[kk]));
-            const float2 act = fma2(half2, th, half2);
-            const float2 sp = mul2(act, fma2(nhalf2, th, half2));
-            const float2 dz = mul2(fma2(an2[kk], we2[kk], mul2(ad2[kk], wp2[kk])), sp);
-            G0[kk] = fma2(an2[kk], act, G0[kk]);
-            G1[kk] = fma2(ad2[kk], act, G1[kk]);
+            // tanh space (as in the register-resident backward): tn = tanh(-z/2),
+            // staged a' = -a/4:  dL/dz = (a'_n w_erev + a'_d w_pos)(tn^2 - 1),
+            // a act = a/2 + 2 a' tn (the a/2 part comes from the per-row sums)
+            const float2 tn = tanh2(fma2(sl2[kk], vp2, nm2[kk]));
+            const float2 dz = mul2(fma2(an2[kk], we2[kk], mul2(ad2[kk], wp2[kk])), fma2(tn, tn, m1));
+            G0[kk] = fma2(an2[kk], tn, G0[kk]);
+            G1[kk] = fma2(ad2[kk], tn, G1[kk]);
             G2[kk] = add2(G2[kk], dz);
             G3[kk] = fma2(dz, vp2, G3[kk]);
             dv = fma2(dz, sl2[kk], dv);
@@ -417,7 +422,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
         if (s < nvalid && pvalid) {
           const long long bs = b0 + s;
           const long long o = bs * HP + p;
-          float gval = fmaf(2.0f, DV[s * NEUR + rl], dirv[j]);  // sl holds sigma/2
+          float gval = fmaf(-2.0f, DV[s * NEUR + rl], dirv[j]);  // sl holds -sigma/2
           if (k == 0) {
             const long long row = bs * T + t;
             a.gsn[row * H + p] = gsnv[j];
@@ -437,12 +442,14 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
           gcm = fmaf(an, vin - vout, gcm);
           ggl = fmaf(an, vl - vout, ggl);
           gvl = fmaf(an, gl, gvl);
+          san += an;
+          sad += ad;
           const bool first = k == 0;
           GSNg[o] = first ? an : gsnv[j] + an;
           GSDg[o] = first ? ad : gsdv[j] + ad;
           DIRg[o] = an * cm;
-          ANg[((n - 1) & 1) * SB_ + o] = an;
-          ADg[((n - 1) & 1) * SB_ + o] = ad;
+          ANg[((n - 1) & 1) * SB_ + o] = -0.25f * an;
+          ADg[((n - 1) & 1) * SB_ + o] = -0.25f * ad;
         }
       }
     }
@@ -458,12 +465,14 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
     gcm += __shfl_xor_sync(0xffffffffu, gcm, stride);
     ggl += __shfl_xor_sync(0xffffffffu, ggl, stride);
     gvl += __shfl_xor_sync(0xffffffffu, gvl, stride);
+    san += __shfl_xor_sync(0xffffffffu, san, stride);
+    sad += __shfl_xor_sync(0xffffffffu, sad, stride);
   }
-  if (ql == 0) {
-    float* pn = a.partn + (long long)grp * 3 * HP;
-    pn[p] = a.accumulate ? pn[p] + gcm : gcm;
-    pn[HP + p] = a.accumulate ? pn[HP + p] + ggl : ggl;
-    pn[2 * HP + p] = a.accumulate ? pn[2 * HP + p] + gvl : gvl;
+  if (ql == 0) {  // 5 rows: the tanh-space layout (+ sum a_n, sum a_d per neuron)
+    float* pn = a.partn + (long long)grp * 5 * HP;
+    const float v[5] = {gcm, ggl, gvl, san, sad};
+#pragma unroll
+    for (int k = 0; k < 5; ++k) pn[k * HP + p] = a.accumulate ? pn[k * HP + p] + v[k] : v[k];
   }
 }
 
@@ -536,6 +545,7 @@ void plan_stream(RecPlan& p, int B, int H, int num_sms) {
   p.smem_fwd = (size_t)2 * kPC * NEUR * 16 + (size_t)2 * ns * kPC * 4;
   p.smem_bwd = (size_t)fixed + (size_t)4 * ns * QC * 4 +
                (size_t)3 * ns * NEUR * 4;
+  p.tanh_space = true;
   p.scratch_fwd = (size_t)2 * B * HP;
   p.scratch_bwd = (size_t)7 * B * HP;
 }
