@@ -25,6 +25,20 @@ namespace cg = cooperative_groups;
 
 namespace ltc {
 
+#ifdef LTC_STREAM_PROF
+// Phase profile of the streamed backward (variant builds only): SM cycles summed
+// over CTAs, measured by thread 0: [0] unfold start..first wait, [1] waits for
+// staged chunks (+ barrier), [2] chunk math, [3] post-loop barrier, [4] tails,
+// [5] cluster barrier, [6] unfolds, [7] issue of the next chunk's copies (inside [2]).
+__device__ unsigned long long g_stream_prof[8];
+#define LTC_PROF_T(v) const long long v = clock64()
+#define LTC_PROF_ADD(i, d) \
+  if (threadIdx.x == 0) atomicAdd(&g_stream_prof[i], (unsigned long long)(d))
+#else
+#define LTC_PROF_T(v)
+#define LTC_PROF_ADD(i, d)
+#endif
+
 namespace {
 
 constexpr int kCL = 8;    // CTAs per cluster
@@ -313,15 +327,22 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   const float2 m1 = make_float2(-1.f, -1.f);
   int t = T - 1, k = U - 1;
   for (int n = NTU - 1; n >= 0; --n) {
+    LTC_PROF_T(p_u0);
     for (int i = tid; i < ns * NEUR; i += kNT) DV[i] = 0.f;
     const float* VP = VPb + (n & 1) * ns * NEUR;       // V[n], staged one unfold ahead
     const float* VPm = VPb + ((n + 1) & 1) * ns * NEUR;  // V[n-1], staged now for the tails
     if (n >= 1) stage_vp(n - 1);
     stage(n, 0, 0);
+    LTC_PROF_T(p_u1);
+    LTC_PROF_ADD(0, p_u1 - p_u0);
     for (int c = 0; c < NC; ++c) {
+      LTC_PROF_T(p_c0);
       cp_async_wait_all();
       __syncthreads();
+      LTC_PROF_T(p_c1);
+      LTC_PROF_ADD(1, p_c1 - p_c0);
       if (c + 1 < NC) stage(n, c + 1, (c + 1) & 1);
+      LTC_PROF_ADD(7, clock64() - p_c1);
       const int buf = c & 1;
       float2 sl2[4], nm2[4], wp2[4], we2[4], G0[4], G1[4], G2[4], G3[4];
       const float4* pk = pks + buf * 8 * kPS + tid;
@@ -392,8 +413,12 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
         *reinterpret_cast<float4*>(gdst + 2 * hp2 + 4 * h2) = make_float4(G2[k0].x, G2[k0].y, G2[k1].x, G2[k1].y);
         *reinterpret_cast<float4*>(gdst + 3 * hp2 + 4 * h2) = make_float4(G3[k0].x, G3[k0].y, G3[k1].x, G3[k1].y);
       }
+      LTC_PROF_ADD(2, clock64() - p_c1);
     }
+    LTC_PROF_T(p_t0);
     __syncthreads();
+    LTC_PROF_T(p_t1);
+    LTC_PROF_ADD(3, p_t1 - p_t0);
     // per-neuron tails of the own rows, samples s = ql + j*QL.  All global loads
     // of the thread's samples are issued first (the chunk registers are dead
     // here), then the math and stores run: the L2 latencies overlap instead of
@@ -453,7 +478,12 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
         }
       }
     }
+    LTC_PROF_T(p_s0);
+    LTC_PROF_ADD(4, p_s0 - p_t1);
     cluster.sync();  // release a_n/a_d of unfold n-1 / acquire the peers'
+    LTC_PROF_T(p_s1);
+    LTC_PROF_ADD(5, p_s1 - p_s0);
+    LTC_PROF_ADD(6, p_s1 - p_u0);
     if (--k < 0) {
       k = U - 1;
       --t;
@@ -558,5 +588,11 @@ cudaError_t launch_stream_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_
   return p.HP == 256 ? launch_cluster8(rec_bwd_stream<32>, a, p.grid_bwd, p.smem_bwd, st)
                      : launch_cluster8(rec_bwd_stream<64>, a, p.grid_bwd, p.smem_bwd, st);
 }
+
+#ifdef LTC_STREAM_PROF
+extern "C" int ltc_debug_stream_prof(unsigned long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, g_stream_prof, sizeof(g_stream_prof));
+}
+#endif
 
 }  // namespace ltc
