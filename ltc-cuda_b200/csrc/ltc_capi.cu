@@ -349,9 +349,9 @@ int ltc_preamble_backward(int64_t rows, int32_t D, const float* x, const float* 
 }
 
 int ltc_wait_timeouts(void) {
-  int n = 0;
-  if (ltc::read_wait_timeouts(&n) != 0) return -1;
-  return n;
+  int n = 0, m = 0;
+  if (ltc::read_wait_timeouts(&n) != 0 || ltc::read_stream_wait_timeouts(&m) != 0) return -1;
+  return n + m;
 }
 
 int64_t ltc_launch_count(void) {
@@ -463,6 +463,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
 
   PackArgs pa = pack_args(dims, params, HP);
   pa.pack = b.pack; pa.packT = b.packT; pa.spack = b.spack; pa.nrn = b.nrn;
+  pa.packT_qc = stream_chunk_cols(L.rp);
   cudaError_t e;
   {
     TimedLaunch tl(LTC_KERNEL_PACK_BWD, st);
@@ -661,6 +662,7 @@ cudaError_t step_unfold_fwd(const LtcDims* d, const LtcParams* p, const Layout& 
   PackArgs pa = pack_args(d, p, L.rp.HP);
   pa.ssig = nullptr;  // recurrent + per-neuron packs only
   pa.pack = b.pack; pa.packT = b.packT; pa.nrn = b.nrn;
+  pa.packT_qc = stream_chunk_cols(L.rp);
   cudaError_t e = launch_pack(pa, st);
   if (e != cudaSuccess) return e;
   RecFwdArgs ra{};

@@ -35,7 +35,10 @@ struct PackArgs {
   const float* gl;      // (H)
   const float* vl;      // (H)
   float4* pack;         // [HP][HP]  (sh, nh, w_pos, w_erev) indexed [p][q]
-  float4* packT;        // [HP][HP]  same, indexed [q][p]   (may be null)
+  float4* packT;        // [HP][HP]  same, indexed [q][p]   (may be null); see packT_qc
+  int packT_qc;         // > 0: packT instead holds pack in rows [p] with each qc-column chunk
+                        //      reordered from (ql, j) = (c/8, c%8) to (j, ql): the streamed
+                        //      backward's TMA staging layout (qc = its chunk width)
   float4* spack;        // [D][HP]   (sh, nh, sw, sw*serev)
   float4* nrn;          // [HP]      (cm, gl, vl, gl*vl)
   int D, H, HP;
@@ -127,10 +130,13 @@ struct RecPlan {
   size_t smem_bwd;
 };
 RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide);
+// chunk width of the streamed backward (256 threads, 8-CTA clusters), 0 on other paths
+inline int stream_chunk_cols(const RecPlan& p) { return p.streamed ? 16384 / p.HP : 0; }
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
 cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st);
 // bounded cluster waits that expired on the current device (ltc_recurrent.cu)
 int read_wait_timeouts(int* count);
+int read_stream_wait_timeouts(int* count);  // ltc_recurrent_stream.cu
 
 // ---- deterministic reductions and final gradient transforms --------------
 struct FinishArgs {

@@ -25,7 +25,14 @@ __global__ void pack_kernel(PackArgs a) {
         v.w = a.w_erev[j];
       }
       a.pack[i] = v;
-      if (a.packT) a.packT[(long long)q * a.HP + p] = v;
+      if (a.packT) {
+        if (a.packT_qc > 0) {
+          const int qc = a.packT_qc, c = q % qc;
+          a.packT[(long long)p * a.HP + (q - c) + (c % 8) * (qc / 8) + c / 8] = v;
+        } else {
+          a.packT[(long long)q * a.HP + p] = v;
+        }
+      }
     } else if (i < nrec + nsen) {
       const long long k = i - nrec;
       const int d = (int)(k / a.HP), q = (int)(k % a.HP);

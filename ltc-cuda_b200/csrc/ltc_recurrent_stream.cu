@@ -17,13 +17,21 @@
 // exchanged through global memory (L2) and ordered by the hardware cluster
 // barrier (release/acquire at cluster scope), one barrier per unfold.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
+#include <mutex>
+
+#include "ltc_cluster.cuh"
 #include "ltc_common.cuh"
 #include "ltc_internal.h"
 
 namespace cg = cooperative_groups;
 
 namespace ltc {
+
+// bounded waits of the streamed backward that expired (see ltc_cluster.cuh)
+__device__ int g_stream_wait_timeouts = 0;
 
 #ifdef LTC_STREAM_PROF
 // Phase profile of the streamed backward (variant builds only): SM cycles summed
@@ -46,8 +54,36 @@ constexpr int kNT = 256;  // threads per CTA
 constexpr int kPC = 32;   // presynaptic rows per forward chunk
 constexpr int kSB = 4;    // samples per register block (backward)
 constexpr int kMaxTailSamples = 96;
-constexpr int kPS = kNT + 1;  // padded pack row (float4) of the backward's chunk staging
-constexpr int kGS = kNT + 4;  // padded gradient row (float4)  // samples per group the backward's tail handles (ns cap)
+
+// Backward launch parameters: the scalar arguments plus the TMA descriptors of the
+// four streamed operands (encoded on the host per launch; the kernel reads them
+// from the grid-constant parameter space).
+struct StreamBwdParams {
+  RecBwdArgs a;
+  CUtensorMap tm_pack;  // chunk-reordered gate pack (packT, see PackArgs::packT_qc) as
+                        // [HP rows][4*HP floats]; box {4*QC, NEUR}
+  CUtensorMap tm_slab;  // gradient slabs as [slots*4*HP rows][HP floats]; box {QC, NEUR}
+  CUtensorMap tm_an;    // a'_n scratch as [2][B][HP] floats; box {QC, ns, 1} (rows >= B read 0)
+  CUtensorMap tm_ad;    // a'_d scratch, same
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_addr(dst)), "l"(tm), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)), "l"(tm), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+// generic-proxy global writes (slab write-back, adjoint scratch) before later
+// async-proxy (TMA) reads of the same memory
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}  // samples per group the backward's tail handles (ns cap)
 
 template <int NEUR>
 struct SGeom {
@@ -183,23 +219,25 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_stream(RecFwdArgs a) {
 // --------------------------------------------------------------------------- backward
 // scratch layout: AN, AD [2][B][HP] (by unfold parity), DIR, GSN, GSD [B][HP]
 template <int NEUR>
-__global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
+__global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(const __grid_constant__ StreamBwdParams P) {
   using G = SGeom<NEUR>;
   constexpr int HP = G::HP, QL = G::QL, QC = G::QC, NC = HP / QC;
   using LR = LaneReduce<QL, kSB>;
-  extern __shared__ __align__(16) float smem[];
+  const RecBwdArgs& a = P.a;
+  extern __shared__ __align__(16) float smem_raw[];
+  // TMA destinations must be 128-byte aligned
+  float* smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int ns = a.ns;
-  // pack / gradient chunks are staged thread-major ([slot][thread]) so that each
-  // thread's 8 synapses are read without bank conflicts
-  // pack / gradient rows are padded (kPS, kGS float4) so that the coalesced
-  // staging copies (consecutive threads = consecutive global addresses) also
-  // write shared memory without bank conflicts
-  float4* pks = reinterpret_cast<float4*>(smem);        // [2][8][kPS]   (pack of synapse j)
-  float* gch = smem + 2 * 8 * kPS * 4;                  // [2][4][2][kGS] float4 (sums k, j-half)
-  float* anc = gch + 2 * 8 * kGS * 4;                   // [2][ns][QC]
-  float* adc = anc + 2 * ns * QC;                       // [2][ns][QC]
+  // chunk c of the CTA's rows, staged by TMA (one thread issues, an mbarrier per
+  // buffer counts the bytes), dense row-major as in global memory
+  float4* pks = reinterpret_cast<float4*>(smem);        // [2][NEUR][QC]  gate pack
+  float* gch = smem + 2 * NEUR * QC * 4;                // [2][4][NEUR][QC] gradient sums
+  float* anc = gch + 2 * 4 * NEUR * QC;                 // [2][ns][QC]  a'_n
+  float* adc = anc + 2 * ns * QC;                       // [2][ns][QC]  a'_d
   float* DV = adc + 2 * ns * QC;                        // [ns][NEUR]
   float* VPb = DV + ns * NEUR;                          // [2][ns][NEUR]: V[m] of the own rows, slot m&1
+  __shared__ __align__(8) uint64_t cbar[2];
+  __shared__ int cabort;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, lane = tid & 31;
@@ -224,13 +262,15 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
   const bool pvalid = p < H;
   float gcm = 0.f, ggl = 0.f, gvl = 0.f, san = 0.f, sad = 0.f;
 
-  // adjoint rows of padded samples in the last register block must read as 0
+  // adjoint rows of padded samples (b >= B, last group only) arrive as zeros from
+  // the TMA's out-of-range fill
   const int nblk = (nvalid + kSB - 1) / kSB;
-  for (int i = tid; i < 2 * (nblk * kSB - nvalid) * QC; i += kNT) {
-    const int buf = i / ((nblk * kSB - nvalid) * QC), rem = i % ((nblk * kSB - nvalid) * QC);
-    const int s = nvalid + rem / QC, cc = rem % QC;
-    anc[(buf * ns + s) * QC + cc] = 0.f;
-    adc[(buf * ns + s) * QC + cc] = 0.f;
+  const uint32_t chunk_bytes = (uint32_t)(NEUR * QC * 16 + 4 * NEUR * QC * 4 + 2 * ns * QC * 4);
+  if (tid == 0) {
+    cabort = (smem_addr(smem) & 127u) != 0;  // never true with the rounding above
+    mbar_init(smem_addr(&cbar[0]), 1);
+    mbar_init(smem_addr(&cbar[1]), 1);
+    mbar_init_fence();
   }
   // padded rows / samples of both V slots stay 0 (only valid entries are staged)
   for (int i = tid; i < 2 * ns * NEUR; i += kNT) VPb[i] = 0.f;
@@ -292,35 +332,23 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       }
     }
   }
+  cp_async_wait_all();  // V[NTU-1] of the own rows
+  fence_proxy_async_global();  // slab zeros and adjoints before the TMA reads
   cluster.sync();
 
-  auto stage = [&](int n, int c, int buf) {
-    // thread th = (row th/QL, lane th%QL) owns columns c*QC + (th%QL)*8 + j;
-    // copies walk the chunk row by row (coalesced) and scatter into that layout
-    float4* pd = pks + buf * 8 * kPS;
-    for (int i = tid; i < NEUR * QC; i += kNT) {
-      const int rw = i / QC, col = i % QC;
-      cp_async16(pd + (col % 8) * kPS + rw * QL + col / 8, a.pack + (long long)(nb + rw) * HP + c * QC + col);
+  auto stage = [&](int n, int c, int buf) {  // chunk c of unfold n -> buffer buf
+    if (tid == 0 && !cabort) {
+      const uint32_t bar = smem_addr(&cbar[buf]);
+      mbar_arm(bar, chunk_bytes);
+      tma_load_2d(pks + buf * NEUR * QC, &P.tm_pack, c * QC * 4, nb, bar);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        tma_load_2d(gch + (buf * 4 + k) * NEUR * QC, &P.tm_slab, c * QC, (grp * 4 + k) * HP + nb, bar);
+      tma_load_3d(anc + buf * ns * QC, &P.tm_an, c * QC, b0, n & 1, bar);
+      tma_load_3d(adc + buf * ns * QC, &P.tm_ad, c * QC, b0, n & 1, bar);
     }
-    float4* gd = reinterpret_cast<float4*>(gch) + buf * 8 * kGS;
-    for (int i = tid; i < NEUR * QC; i += kNT) {
-      const int k = i / (NEUR * QC / 4), rem = i % (NEUR * QC / 4);
-      const int rw = rem / (QC / 4), c4 = rem % (QC / 4);  // columns 4*c4 .. 4*c4+3
-      cp_async16(gd + (k * 2 + c4 % 2) * kGS + rw * QL + c4 / 2,
-                 slab + k * hp2 + (long long)(nb + rw) * HP + c * QC + 4 * c4);
-    }
-    const float* asrc = ANg + (n & 1) * SB_;
-    const float* dsrc = ADg + (n & 1) * SB_;
-    float* ad_ = anc + buf * ns * QC;
-    float* dd_ = adc + buf * ns * QC;
-    for (int i = tid; i < nvalid * (QC / 4); i += kNT) {
-      const int s = i / (QC / 4), c4 = i % (QC / 4);
-      const long long o = (long long)(b0 + s) * HP + c * QC + 4 * c4;
-      cp_async16(ad_ + s * QC + 4 * c4, asrc + o);
-      cp_async16(dd_ + s * QC + 4 * c4, dsrc + o);
-    }
-    cp_async_commit();
   };
+  uint32_t cphase = 0;  // parity bit per buffer
 
   const int own = LR::own_base(lane);
   const bool writer = LR::writer(lane);
@@ -331,25 +359,30 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
     for (int i = tid; i < ns * NEUR; i += kNT) DV[i] = 0.f;
     const float* VP = VPb + (n & 1) * ns * NEUR;       // V[n], staged one unfold ahead
     const float* VPm = VPb + ((n + 1) & 1) * ns * NEUR;  // V[n-1], staged now for the tails
-    if (n >= 1) stage_vp(n - 1);
+    if (n >= 1) {
+      stage_vp(n - 1);
+      cp_async_commit();
+    }
     stage(n, 0, 0);
     LTC_PROF_T(p_u1);
     LTC_PROF_ADD(0, p_u1 - p_u0);
     for (int c = 0; c < NC; ++c) {
       LTC_PROF_T(p_c0);
-      cp_async_wait_all();
-      __syncthreads();
+      const int buf = c & 1;
+      mbar_wait(smem_addr(&cbar[buf]), (cphase >> buf) & 1u, &cabort, &g_stream_wait_timeouts);
+      cphase ^= 1u << buf;
+      __syncthreads();  // everyone is past chunk c-1: its buffer takes chunk c+1
       LTC_PROF_T(p_c1);
       LTC_PROF_ADD(1, p_c1 - p_c0);
       if (c + 1 < NC) stage(n, c + 1, (c + 1) & 1);
       LTC_PROF_ADD(7, clock64() - p_c1);
-      const int buf = c & 1;
       float2 sl2[4], nm2[4], wp2[4], we2[4], G0[4], G1[4], G2[4], G3[4];
-      const float4* pk = pks + buf * 8 * kPS + tid;
-      const float4* gs = reinterpret_cast<const float4*>(gch) + buf * 8 * kGS + tid;
+      // reordered chunk: synapse j of lane ql at j*QL + ql (2-way bank conflicts at most)
+      const float4* pk = pks + buf * NEUR * QC + rl * QC + ql;
+      const float* gs = gch + buf * 4 * NEUR * QC + rl * QC + ql * 8;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const float4 p0 = pk[(2 * kk) * kPS], p1 = pk[(2 * kk + 1) * kPS];
+        const float4 p0 = pk[(2 * kk) * QL], p1 = pk[(2 * kk + 1) * QL];
         // negated half-scale constants: the gate argument is -z/2, so tanh gives -t
         sl2[kk] = make_float2(-p0.x, -p1.x);
         nm2[kk] = make_float2(-p0.y, -p1.y);
@@ -358,8 +391,10 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       }
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
-        const float4 g0 = gs[(0 + h2) * kGS], g1 = gs[(2 + h2) * kGS];
-        const float4 g2 = gs[(4 + h2) * kGS], g3 = gs[(6 + h2) * kGS];
+        const float4 g0 = *reinterpret_cast<const float4*>(gs + 4 * h2);
+        const float4 g1 = *reinterpret_cast<const float4*>(gs + NEUR * QC + 4 * h2);
+        const float4 g2 = *reinterpret_cast<const float4*>(gs + 2 * NEUR * QC + 4 * h2);
+        const float4 g3 = *reinterpret_cast<const float4*>(gs + 3 * NEUR * QC + 4 * h2);
         G0[2 * h2] = make_float2(g0.x, g0.y); G0[2 * h2 + 1] = make_float2(g0.z, g0.w);
         G1[2 * h2] = make_float2(g1.x, g1.y); G1[2 * h2 + 1] = make_float2(g1.z, g1.w);
         G2[2 * h2] = make_float2(g2.x, g2.y); G2[2 * h2 + 1] = make_float2(g2.z, g2.w);
@@ -416,6 +451,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
       LTC_PROF_ADD(2, clock64() - p_c1);
     }
     LTC_PROF_T(p_t0);
+    cp_async_wait_all();  // V[n-1] for the tails
     __syncthreads();
     LTC_PROF_T(p_t1);
     LTC_PROF_ADD(3, p_t1 - p_t0);
@@ -480,6 +516,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(RecBwdArgs a) {
     }
     LTC_PROF_T(p_s0);
     LTC_PROF_ADD(4, p_s0 - p_t1);
+    fence_proxy_async_global();  // slab write-back and a'_n/a'_d before the TMA reads
     cluster.sync();  // release a_n/a_d of unfold n-1 / acquire the peers'
     LTC_PROF_T(p_s1);
     LTC_PROF_ADD(5, p_s1 - p_s0);
@@ -554,7 +591,7 @@ void plan_stream(RecPlan& p, int B, int H, int num_sms) {
   // resident clusters as that cap forces, the samples spread evenly over them
   constexpr int kNspt[] = {1, 2, 3, 4, 6, 8, 12, 16, 18, 20, 24};
   constexpr int kNn = sizeof(kNspt) / sizeof(kNspt[0]);
-  const long long fixed = (long long)2 * 8 * kPS * 16 + (long long)2 * 8 * kGS * 16;
+  const long long fixed = (long long)2 * NEUR * QC * 16 + (long long)2 * 4 * NEUR * QC * 4 + 128;
   int ns_cap = (int)((227LL * 1024 - 1024 - fixed) / (16 * QC + 12 * NEUR));
   if (ns_cap > kMaxTailSamples) ns_cap = kMaxTailSamples;
   int top = 0;  // largest instantiated count within the cap
@@ -584,9 +621,59 @@ cudaError_t launch_stream_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_
   return p.HP == 256 ? fwd_dispatch<32>(a, p, st) : fwd_dispatch<64>(a, p, st);
 }
 
+namespace {
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode_f32(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                const cuuint32_t* box) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u)) return false;
+  const cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
 cudaError_t launch_stream_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st) {
-  return p.HP == 256 ? launch_cluster8(rec_bwd_stream<32>, a, p.grid_bwd, p.smem_bwd, st)
-                     : launch_cluster8(rec_bwd_stream<64>, a, p.grid_bwd, p.smem_bwd, st);
+  const int HP = p.HP, NEUR = HP / kCL, QC = (kNT / NEUR) * 8;
+  const int slots = p.grid_bwd / kCL;
+  StreamBwdParams P;
+  memset(&P, 0, sizeof(P));
+  P.a = a;
+  const float* ANg = a.scratch;
+  const float* ADg = ANg + 2 * (size_t)a.B * HP;
+  const cuuint64_t dp[2] = {(cuuint64_t)HP * 4, (cuuint64_t)HP};
+  const cuuint64_t sp[1] = {(cuuint64_t)HP * 16};
+  const cuuint32_t bp[2] = {(cuuint32_t)QC * 4, (cuuint32_t)NEUR};
+  const cuuint64_t ds[2] = {(cuuint64_t)HP, (cuuint64_t)slots * 4 * HP};
+  const cuuint64_t ss[1] = {(cuuint64_t)HP * 4};
+  const cuuint32_t bs[2] = {(cuuint32_t)QC, (cuuint32_t)NEUR};
+  const cuuint64_t da[3] = {(cuuint64_t)HP, (cuuint64_t)a.B, 2};
+  const cuuint64_t sa[2] = {(cuuint64_t)HP * 4, (cuuint64_t)a.B * HP * 4};
+  const cuuint32_t ba[3] = {(cuuint32_t)QC, (cuuint32_t)a.ns, 1};
+  if (!a.packT || !encode_f32(&P.tm_pack, a.packT, 2, dp, sp, bp) || !encode_f32(&P.tm_slab, a.part, 2, ds, ss, bs) ||
+      !encode_f32(&P.tm_an, ANg, 3, da, sa, ba) || !encode_f32(&P.tm_ad, ADg, 3, da, sa, ba))
+    return cudaErrorInvalidValue;  // no launch with a descriptor that did not encode
+  return HP == 256 ? launch_cluster8(rec_bwd_stream<32>, P, p.grid_bwd, p.smem_bwd, st)
+                   : launch_cluster8(rec_bwd_stream<64>, P, p.grid_bwd, p.smem_bwd, st);
+}
+
+int read_stream_wait_timeouts(int* count) {
+  return (int)cudaMemcpyFromSymbol(count, g_stream_wait_timeouts, sizeof(int));
 }
 
 #ifdef LTC_STREAM_PROF
