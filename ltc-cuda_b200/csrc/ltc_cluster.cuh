@@ -8,10 +8,11 @@
 // A CTA starts the next unfold once its own mbarrier has seen the expected
 // number of bytes: no cluster-wide barrier and no fence per unfold.
 //
-// Protocol for a double-buffered vector (slots 0/1, one mbarrier per slot):
-//   * init (thread 0): mbarrier.init(count 1) for both slots, fence, arm both slots
-//     with expect_tx(bytes of one phase); then one cluster barrier before the
-//     first remote store.
+// Protocol for a double-buffered vector (slots 0/1; the kernels keep one mbarrier
+// per (slot, 4-sample block), so each block is its own instance of this protocol):
+//   * init (thread 0): mbarrier.init(count 1) for every slot, fence, arm each with
+//     expect_tx(bytes of one phase); then one cluster barrier before the first
+//     remote store.
 //   * producer: every (neuron, sample) item of the cluster's sample group is sent
 //     by exactly one lane to every CTA (zeros for padding), so each phase
 //     receives exactly the armed byte count.
@@ -22,8 +23,9 @@
 //     sends data of phase k+1 only after it received all of phase k+1's inputs,
 //     which every CTA produces only after having waited phase k.
 //   * every wait is bounded (about 2 s of SM clock); on expiry the kernel counts a
-//     timeout in a device counter (read by ltc_wait_timeouts()), stops waiting for the rest of the launch
-//     (results are then garbage and the host reports the error) and still exits.
+//     timeout in a device counter (read by ltc_wait_timeouts()), stops waiting for
+//     the rest of the launch (its results are then invalid) and still exits.
+// The streamed backward reuses mbar_* for its TMA chunk arrivals (local bytes only).
 #pragma once
 
 #include <stdint.h>
