@@ -264,7 +264,7 @@ def test_streaming_inference_matches_full_sequence():
     assert torch.equal(state[0], hf)
 
 
-@pytest.mark.parametrize("B,H", [(9000, 64), (5000, 128)])
+@pytest.mark.parametrize("B,H", [(9000, 64), (5000, 128), (1500, 256)])
 def test_multi_wave_grid_vs_oracle(B, H):
     """Batches beyond one wave of resident sample groups (the per-CTA sample count is
     capped by shared memory) run as several waves; check them against the oracle."""
