@@ -12,7 +12,11 @@
 //             L2: 4*NEUR*HP floats per CTA), thread = (row, 8 columns), and
 //             accumulates every synapse over all ns samples in registers before
 //             writing the chunk back -- one read-modify-write per synapse per
-//             unfold for the whole sample group.
+//             unfold for the whole sample group.  Its chunks (pack slice, 4 slab
+//             tiles, a'_n / a'_d tiles) arrive by TMA tensor copies that one
+//             thread issues, counted on an mbarrier per buffer, so the compute
+//             warps never stall on copy issue; generic writes that a later TMA
+//             reads are fenced with fence.proxy.async before the cluster barrier.
 // Per-neuron vectors (state in the forward; a_n, a_d in the backward) are
 // exchanged through global memory (L2) and ordered by the hardware cluster
 // barrier (release/acquire at cluster scope), one barrier per unfold.
