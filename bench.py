@@ -48,8 +48,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c3", choices=sorted(synth.CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_cuda"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reference-cuda", type=int, default=1,
+                    help="1 (default, N=1 only): also time the reference's own CUDA kernels in a child process")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=None,
                     help="override the configuration's global batch (profiling captures of smaller cases)")
@@ -126,24 +128,56 @@ def physical_gpu_index(local_rank: int) -> int:
 
 
 # --------------------------------------------------------------------------- CPU arm
-def cpu_sample_rate(cfg, seconds: float, threads: int):
-    """Oracle port (restatement of the reference TorchScript path) timed on host cores:
-    module-level fwd+bwd with sum loss on a bounded batch/time slice of the workload."""
-    from oracle import ltc_oracle as orc
+# Batch/time slice of each configuration that the CPU arms time (samples are
+# independent, so B*T/s on a slice is the rate of the whole workload).  The
+# cpu_baseline leg of the GPU arm and the --impl reference arm use the same slice.
+CPU_SLICE = {"c0": (24, 8), "c1": (16, 32), "c2": (8, 8), "c3": (256, 8), "c4": (1, 2)}
+
+
+def reference_cpu_step(cfg, threads: int):
+    """One fwd+bwd (sum loss) of the reference TorchScript path on a slice, on host cores.
+
+    The reference's own ``ltc.py`` (staged by ``oracle/build_ref.py``) runs when it is
+    present ("reference"); otherwise the oracle's restatement of it ("port")."""
+    from oracle import reference_module as rm
     torch.set_num_threads(threads)
-    Bs = {"c0": 24, "c1": 16, "c2": 8, "c3": 64, "c4": 1}[cfg.name]
-    Ts = {"c0": 8, "c1": 32, "c2": 8, "c3": 8, "c4": 2}[cfg.name]
+    Bs, Ts = CPU_SLICE[cfg.name]
     p, x = synth.make_workload(cfg, batch=Bs)
     x = x[:, :Ts].contiguous()
-    params = {k: v.clone().requires_grad_(k in orc.parameter_names()) for k, v in p.items()}
+    # in the GPU arm's process the module name ltc_cuda is already this package's;
+    # alone, the reference's own loader binds it (and must find its prebuilt kernels
+    # on a CUDA machine rather than start a JIT build)
+    binding = "ours" if "ltc_cuda" in sys.modules else "reference"
+    why = rm.available(cuda=binding == "reference" and torch.cuda.is_available())
+    if why is None:
+        import logging
+        logging.getLogger("ltc").setLevel(logging.ERROR)  # the reference logs its CPU fallback once
+        ltc = rm.import_reference(binding)
+        m = rm.reference_module(ltc, p, cfg.D, cfg.H, cfg.dt, cfg.U, cfg.density, cfg.sensory_density)
 
-    def one():
-        out, _ = orc.module_forward(params, x, None, cfg.dt, cfg.U)
-        out.sum().backward()
-        for v in params.values():
-            v.grad = None
+        def one():
+            out, _ = m(x)  # CPU input: the reference dispatches to its TorchScript solver (ltc.py:293-326)
+            out.sum().backward()
+            m.zero_grad(set_to_none=True)
+        kind, what = "reference", "reference ltc.py TorchScript path (module fwd+bwd, sum loss)"
+    else:
+        from oracle import ltc_oracle as orc
+        params = {k: v.clone().requires_grad_(k in orc.parameter_names()) for k, v in p.items()}
 
-    one()  # warm-up
+        def one():
+            out, _ = orc.module_forward(params, x, None, cfg.dt, cfg.U)
+            out.sum().backward()
+            for v in params.values():
+                v.grad = None
+        kind, what = "port", f"oracle restatement of the reference TorchScript path ({why})"
+    return one, Bs, Ts, kind, what
+
+
+def cpu_sample_rate(cfg, seconds: float, threads: int):
+    """Reference CPU path timed on host cores for about ``seconds`` on the slice."""
+    one, Bs, Ts, kind, what = reference_cpu_step(cfg, threads)
+    one()
+    one()  # warm-up (TorchScript profiles its first calls)
     n, t0 = 0, time.perf_counter()
     while True:
         one()
@@ -151,46 +185,174 @@ def cpu_sample_rate(cfg, seconds: float, threads: int):
         el = time.perf_counter() - t0
         if el >= seconds or n >= 1000:
             break
-    return {"value": n * Bs * Ts / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{cfg.name} slice B={Bs} T={Ts} (D={cfg.D} H={cfg.H} U={cfg.U}), module fwd+bwd sum loss, "
-                      f"{n} reps in {el:.1f}s, oracle restatement of the reference TorchScript path"}
+    return {"value": n * Bs * Ts / el, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{cfg.name} slice B={Bs} T={Ts} (D={cfg.D} H={cfg.H} U={cfg.U}), {what}, "
+                      f"{n} reps in {el:.1f}s"}
 
 
 def run_reference(args, cfg, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    from oracle import ltc_oracle as orc
-    torch.set_num_threads(threads)
-    Bs, Ts = {"c0": (24, 8), "c1": (16, 32), "c2": (8, 8), "c3": (256, 8), "c4": (1, 2)}[cfg.name]
-    p, x = synth.make_workload(cfg, batch=Bs)
-    x = x[:, :Ts].contiguous()
-    params = {k: v.clone().requires_grad_(k in orc.parameter_names()) for k, v in p.items()}
-
-    def step():
-        out, _ = orc.module_forward(params, x, None, cfg.dt, cfg.U)
-        out.sum().backward()
-        for v in params.values():
-            v.grad = None
-
-    for _ in range(args.warmup):
-        step()
+    one, Bs, Ts, kind, what = reference_cpu_step(cfg, threads)
+    for _ in range(max(3, args.warmup)):
+        one()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        one()
     el = time.perf_counter() - t0
     value = args.steps * Bs * Ts / el
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
+            "warmup": max(3, args.warmup), "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": cfg.name, "B": Bs, "T": Ts, "D": cfg.D, "H": cfg.H, "U": cfg.U,
                        "sample_of": {"B": cfg.B, "T": cfg.T}},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{cfg.name} slice B={Bs} T={Ts} per step; CPU restatement of the "
-                                       "reference TorchScript solver (module fwd+bwd, sum loss)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                             "sample": f"{cfg.name} slice B={Bs} T={Ts} per step; {what}"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_reference_cuda(args, cfg, rank):
+    """The reference's own CUDA kernels (csrc/ltc_kernels.cu compiled for sm_100a by
+    oracle/build_ref.py) driven through the reference module, timed like our arm:
+    fwd + sum-loss bwd (+ Adam at c3) per step, L2 flushed between steps, CUDA events."""
+    if rank != 0:
+        return
+    from oracle import reference_module as rm
+    why = rm.available(cuda=True)
+    if why:
+        print(json.dumps({"impl": "reference_cuda", "unavailable": why}), flush=True)
+        return
+    ltc = rm.import_reference("reference")
+    import ltc_cuda as ref_cuda  # the reference loader (oracle/_ref/ltc_cuda.py)
+    if not ref_cuda._HAS_CUDA_KERNELS:
+        print(json.dumps({"impl": "reference_cuda", "unavailable": "reference CUDA extension did not load"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    p, x = synth.make_workload(cfg)
+    m = rm.reference_module(ltc, p, cfg.D, cfg.H, cfg.dt, cfg.U, cfg.density, cfg.sensory_density).to(dev)
+    x = x.to(dev)
+    opt = torch.optim.Adam(m.parameters(), lr=1e-4, fused=True) if cfg.training_step else None
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step():
+        out, _ = m(x)
+        out.sum().backward()
+        if opt is not None:
+            opt.step()
+        m.zero_grad(set_to_none=True)
+
+    # parity of the reference kernels against the reference TorchScript path on a slice
+    par = module_parity(lambda mm, xx: mm(xx), lambda: rm.reference_module(
+        ltc, p, cfg.D, cfg.H, cfg.dt, cfg.U, cfg.density, cfg.sensory_density).to(dev), ltc, p, cfg, dev)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        flush.zero_()
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    line = {"metric": METRIC, "value": cfg.B * cfg.T / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic", "impl": "reference_cuda",
+            "config": {"workload": cfg.name, "B": cfg.B, "T": cfg.T, "D": cfg.D, "H": cfg.H, "U": cfg.U,
+                       "step": "train (fwd+bwd+adam)" if cfg.training_step else "fwd+bwd",
+                       "kernels": "reference csrc/ltc_kernels.cu, nvcc -O3 --use_fast_math sm_100a"},
+            "parity_vs_reference_torchscript": par}
+    print(json.dumps(line), flush=True)
+
+
+PARITY_SLICE = {"c0": (24, 8), "c1": (16, 32), "c2": (8, 64), "c3": (8, 128), "c4": (2, 64)}
+
+
+def module_parity(run_ours, make_ours, ltc, p, cfg, dev):
+    """Module fwd + sum-loss bwd of a candidate against the reference TorchScript path
+    (``_force_torchscript``, ``ltc.py:293-326``) on the GPU, same seeded slice.
+    Bars (north star): forward max-abs 1e-3; gradients rtol 5e-2 / atol 1e-2."""
+    from oracle import reference_module as rm
+    Bs, Ts = PARITY_SLICE[cfg.name]
+    _, x = synth.make_workload(cfg, batch=Bs)
+    x = x[:, :Ts].contiguous().to(dev)
+    ref = rm.reference_module(ltc, p, cfg.D, cfg.H, cfg.dt, cfg.U, cfg.density, cfg.sensory_density).to(dev)
+    ref._force_torchscript = True
+    ro, (rh, _) = ref(x)
+    ro.sum().backward()
+    ours = make_ours()
+    oo, (oh, _) = run_ours(ours, x)
+    oo.sum().backward()
+    fwd = max((oo - ro).abs().max().item(), (oh - rh).abs().max().item())
+    rg = dict(ref.named_parameters())
+    worst, ok = 0.0, True
+    for n, q in ours.named_parameters():
+        a, b = q.grad.double(), rg[n].grad.double()
+        worst = max(worst, ((a - b).abs().max() / b.abs().max().clamp_min(1e-12)).item())
+        ok = ok and bool(torch.allclose(a, b, rtol=5e-2, atol=1e-2))
+    return {"slice": {"B": Bs, "T": Ts}, "fwd_max_abs": fwd, "grad_max_rel": worst,
+            "pass": bool(fwd < 1e-3 and ok), "against": "reference ltc.py TorchScript path on the GPU"}
+
+
+def our_parity(cfg, p, dev):
+    """Parity of this build's module on a slice of the timed configuration, checked
+    before the timed region against the reference TorchScript path (or, where the
+    reference is not staged, the oracle restatement of it)."""
+    import ltc_layer
+    from oracle import reference_module as rm
+
+    def make():
+        m = ltc_layer.TrueLiquidTimeConstant(cfg.D, cfg.H, dt=cfg.dt, ode_unfolds=cfg.U, sparsity=cfg.density,
+                                             sensory_sparsity=cfg.sensory_density)
+        m.load_state_dict(p)
+        return m.to(dev)
+    if rm.available() is None:
+        import logging
+        logging.getLogger("ltc").setLevel(logging.ERROR)
+        ltc = rm.import_reference("ours")
+        return module_parity(lambda mm, xx: mm(xx), make, ltc, p, cfg, dev)
+    from oracle import ltc_oracle as orc
+    Bs, Ts = PARITY_SLICE[cfg.name]
+    _, x = synth.make_workload(cfg, batch=Bs)
+    x = x[:, :Ts].contiguous().to(dev)
+    params = {k: v.to(dev).requires_grad_(k in orc.parameter_names()) for k, v in p.items()}
+    ro, (rh, _) = orc.module_forward(params, x, None, cfg.dt, cfg.U)
+    ro.sum().backward()
+    m = make()
+    oo, (oh, _) = m(x)
+    oo.sum().backward()
+    fwd = max((oo - ro).abs().max().item(), (oh - rh).abs().max().item())
+    worst, ok = 0.0, True
+    for n, q in m.named_parameters():
+        a, b = q.grad.double(), params[n].grad.double()
+        worst = max(worst, ((a - b).abs().max() / b.abs().max().clamp_min(1e-12)).item())
+        ok = ok and bool(torch.allclose(a, b, rtol=5e-2, atol=1e-2))
+    return {"slice": {"B": Bs, "T": Ts}, "fwd_max_abs": fwd, "grad_max_rel": worst,
+            "pass": bool(fwd < 1e-3 and ok), "against": "oracle restatement (reference not staged)"}
+
+
+def reference_cuda_subprocess(name, batch, seq, steps=5, warmup=3, timeout=900):
+    """Run ``--impl reference_cuda`` in a child process (it binds the reference's own
+    ``ltc_cuda`` module name) and return its JSON line, or why it is missing."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference_cuda", "--config", name,
+           "--steps", str(steps), "--warmup", str(warmup)]
+    if batch is not None:
+        cmd += ["--batch", str(batch)]
+    if seq is not None:
+        cmd += ["--seq", str(seq)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"timed out after {timeout} s"}
+    for ln in reversed(r.stdout.strip().splitlines()):
+        if ln.startswith("{"):
+            return json.loads(ln)
+    return {"unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout).strip().splitlines()[-1:]}"}
 
 
 # --------------------------------------------------------------------------- GPU arm
@@ -208,6 +370,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, cfg, rank)
+        return
+    if args.impl == "reference_cuda":
+        sys.path.remove(os.path.join(REPO, "ltc-cuda_b200"))  # the reference binds its own ltc_cuda
+        run_reference_cuda(args, cfg, rank)
         return
 
     import ltc_cuda
@@ -262,6 +428,9 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    parity = None
+    if rank == 0:
+        parity = our_parity(cfg, p, dev)
     for _ in range(max(3, args.warmup)):
         step(x_dev)
     torch.cuda.synchronize()
@@ -386,10 +555,18 @@ def main():
               "recurrent_bwd": Bl * cfg.T * cfg.U * cfg.H * cfg.H,
               "sensory_fwd": Bl * cfg.T * cfg.D * cfg.H,
               "sensory_bwd": Bl * cfg.T * cfg.D * cfg.H}
+    # Work per step of each kernel kind.  Memory-lean training runs the forward
+    # kernels twice per step (the forward, then the recompute inside the backward,
+    # once per segment), so their work per step doubles; every figure below is
+    # work over the window's steps / the kind's total time in the window, so it
+    # does not depend on how many launches a pass is split into.
+    twice = 2 if args.lean else 1
+    work = {k: v * (twice if k.endswith("_fwd") else 1) for k, v in visits.items()}
     dom = max(visits, key=lambda k: ktimes[k][0])
     tot_ms, n_l = ktimes[dom]
     per_launch_s = tot_ms / max(1, n_l) / 1e3
-    achieved = visits[dom] / per_launch_s / 1e9
+    achieved = work[dom] * args.steps / (tot_ms / 1e3) / 1e9
+    ms_per_launch = per_launch_s * 1e3
     peak = sms * 16 / 2 * f_mhz * 1e6 / 1e9  # Gvisits/s: 16 MUFU/clk/SM, 2 MUFU per visit
     # the kernels' own bound: tanh-form gates issue 1 MUFU op per visit; the
     # forward kernels then need 3 FP32 lane-ops per visit (MUFU-bound, 16
@@ -402,11 +579,11 @@ def main():
     S = cfg.D * cfg.H + cfg.U * cfg.H * cfg.H
     t_roof = cfg.B * cfg.T * S * 4 / (16 * sms * f_mhz * 1e6 * world)
     # recurrent kernels alone, same convention (the H=128 north-star figure)
-    per_l = lambda k: ktimes[k][0] / max(1, ktimes[k][1]) / 1e3
+    per_step = lambda k: ktimes[k][0] / args.steps / 1e3  # seconds of kernel kind k per step
     t_roof_rec = Bl * cfg.T * cfg.U * cfg.H * cfg.H * 4 / (16 * sms * f_mhz * 1e6)
-    rec_frac = t_roof_rec / (per_l("recurrent_fwd") + per_l("recurrent_bwd"))
+    rec_frac = t_roof_rec / (per_step("recurrent_fwd") + per_step("recurrent_bwd"))
     # sensory forward: reads x (4 D B per (b,t)), writes sn/sd (8 H B); MUFU-bound, not HBM-bound
-    sens_gbs = Bl * cfg.T * (4 * cfg.D + 8 * cfg.H) / per_l("sensory_fwd") / 1e9
+    sens_gbs = twice * Bl * cfg.T * (4 * cfg.D + 8 * cfg.H) / per_step("sensory_fwd") / 1e9
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -421,7 +598,7 @@ def main():
                    "saved_state": "step boundaries, unfolds recomputed (lean)" if args.lean else "every unfold"},
         "e2e": e2e,
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
-                     "frac": achieved / peak,
+                     "frac": achieved / peak, "ms_per_launch": ms_per_launch,
                      "traffic": (NCU_TRAFFIC_PER_BT[(cfg.name, dom)] * Bl * cfg.T
                                  if (cfg.name, dom) in NCU_TRAFFIC_PER_BT else None),
                      "traffic_unit": "bytes per launch (ncu capture, scaled)",
@@ -439,8 +616,11 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
     }
+    line["parity"] = parity
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample_rate(cfg, args.cpu_seconds, os.cpu_count() or 1)
+    if rank == 0 and world == 1 and args.reference_cuda:
+        line["reference_cuda"] = reference_cuda_subprocess(cfg.name, args.batch, args.seq)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -173,7 +173,8 @@ int ltc_preamble_backward(int64_t rows, int32_t D, const float* x, const float* 
  * are rejected with an error.  The first call on a device resolves the array's
  * address (cudaGetSymbolAddress): make it before any stream capture.  All calls
  * on a device share the array, so calls that overlap on the GPU race: serialise
- * them. */
+ * them.  Its launches create no timing events: they are not counted by
+ * ltc_launch_count() nor timed by ltc_timing_enable(). */
 int ltc_forward_noalloc(const LtcDims* dims, const LtcParams* params, const float* x, const float* h0,
                         float* outputs, float* h_final, ltc_stream_t stream);
 
@@ -202,7 +203,8 @@ enum {
 int ltc_timing_enable(int on);
 int ltc_timing_collect(double* total_ms, int32_t* launches, int n);
 
-/* Number of kernels launched through the library by this process. */
+/* Number of kernels launched through the library by this process (every entry
+ * point except ltc_forward_noalloc). */
 int64_t ltc_launch_count(void);
 
 /* Number of bounded in-kernel waits (the per-unfold exchange between the CTAs

@@ -8,8 +8,7 @@
 //   per-synapse "gate pack" holding the half-scale constants
 //   (sh, nh) = (sigma/2, -sigma*mu/2), so that z/2 = sh*v + nh, as
 //   act = 0.5 + 0.5 * tanh(z/2) with the hardware tanh.approx (one MUFU op).
-//   The forward kernels fold the 0.5 terms into sums of the weights; the
-//   ex2 + reciprocal form (gate / gate_newton below) is kept as a variant.
+//   The forward kernels fold the 0.5 terms into sums of the weights.
 // * Saved forward state for the backward pass:
 //     V[n][b][h], n = t*U + k, n in [0, T*U]: the input of unfold k at step t
 //       (V[T*U] is the final state);
@@ -19,16 +18,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#define LTC_LOG2E 1.4426950408889634f
-#define LTC_LN2 0.6931471805599453f
 
 namespace ltc {
-
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
@@ -72,25 +63,6 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
 }
 __device__ __forceinline__ float2 tanh2(float2 a) { return make_float2(tanh_approx(a.x), tanh_approx(a.y)); }
 
-// act = sigmoid(sigma * (v - mu)) given the ex2-scale constants
-// (sl, nm) = (-sigma*log2 e, sigma*mu*log2 e): ex2 + rcp (2 MUFU).
-__device__ __forceinline__ float gate(float sl, float nm, float v) {
-  return rcp_approx(1.0f + ex2_approx(fmaf(sl, v, nm)));
-}
-
-// Same gate with one MUFU op: the reciprocal 1/(1+e) runs on the FMA pipe as two
-// Newton-Raphson steps r <- r*(2 - d*r) from the classic integer-subtraction seed
-// (bits(r0) = 0x7EF311C7 - bits(d), max relative error 5.1e-2), which leaves a
-// relative error <= 6.7e-6 for every d in [1, 2^64].  y is clamped to 64 so that
-// d stays finite (act < 6e-20 there, i.e. 0 to fp32 accuracy).
-__device__ __forceinline__ float gate_newton(float sl, float nm, float v) {
-  const float d = 1.0f + ex2_approx(fminf(fmaf(sl, v, nm), 64.0f));
-  float r = __int_as_float(0x7EF311C7 - __float_as_int(d));
-  r = r * fmaf(-d, r, 2.0f);
-  r = r * fmaf(-d, r, 2.0f);
-  return r;
-}
-
 // Backward-pass gate with one MUFU op: sigmoid(z) = 0.5 + 0.5*tanh(z/2), given the
 // half-scale pack (sh, nh) = (sigma/2, -sigma*mu/2) so that z/2 = sh*v + nh.
 // tanh.approx has a relative error of about 2^-11; the adjoint tolerates it
@@ -98,8 +70,6 @@ __device__ __forceinline__ float gate_newton(float sl, float nm, float v) {
 __device__ __forceinline__ float gate_tanh(float sh, float nh, float v) {
   return fmaf(0.5f, tanh_approx(fmaf(sh, v, nh)), 0.5f);
 }
-// half-scale pack (sh, nh)  ->  ex2-scale (sl, nm) = (-sigma*log2 e, sigma*mu*log2 e)
-#define LTC_EX2_SCALE (-2.0f * LTC_LOG2E)
 
 // ---------------------------------------------------------------------------
 // Transposed reduction across the TPC lanes that share one neuron.

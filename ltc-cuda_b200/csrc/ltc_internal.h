@@ -5,20 +5,6 @@
 #include <stddef.h>
 #include <stdint.h>
 
-// Number of the 8 synapses per thread whose forward gate uses the MUFU reciprocal
-// (the others use the FMA-pipe Newton reciprocal); tuned on B200.
-#ifndef LTC_FWD_MUFU_RCP
-#define LTC_FWD_MUFU_RCP 2
-#endif
-
-// 1 (default): the register-resident forward kernel evaluates its gates with one
-// tanh.approx each; 0: ex2 + reciprocal (MUFU / FMA-pipe Newton), kept as a
-// reference variant.  Measured forward error on B200 is ~1e-6 either way (the
-// leak/capacitance term dominates the denominator, so gate errors shrink).
-#ifndef LTC_FWD_TANH
-#define LTC_FWD_TANH 1
-#endif
-
 namespace ltc {
 
 // ---- parameter packing --------------------------------------------------

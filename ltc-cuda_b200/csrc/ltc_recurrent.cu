@@ -64,15 +64,6 @@ struct Geometry {
   __device__ __forceinline__ static int sub(int j, int g) { return (j / 4) * (HP / 2) + 4 * g + (j % 4); }
 };
 
-#if !LTC_FWD_TANH
-// Gate of synapse j in the forward kernels: synapses j < kMufuRcp use the MUFU
-// reciprocal, the rest the FMA-pipe Newton reciprocal, balancing the two pipes.
-constexpr int kMufuRcp = LTC_FWD_MUFU_RCP;
-
-__device__ __forceinline__ float fwd_gate(int j, float sl, float nm, float v) {
-  return j < kMufuRcp ? gate(sl, nm, v) : gate_newton(sl, nm, v);
-}
-#endif
 
 // Cluster helpers: with CL > 1 the CTAs of a cluster share one sample group and
 // each owns HP/CL neurons; per-neuron results of an unfold are sent to every
@@ -127,15 +118,6 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
       const float4 pk = a.pack[G::sub(j, g) * HP + c + r * NG];
       sl[r][j] = pk.x; nm[r][j] = pk.y; wp[r][j] = pk.z; we[r][j] = pk.w;
     }
-#if !LTC_FWD_TANH
-#pragma unroll
-  for (int r = 0; r < RPT; ++r)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {  // half-scale pack -> ex2-scale pack
-      sl[r][j] *= LTC_EX2_SCALE;
-      nm[r][j] *= LTC_EX2_SCALE;
-    }
-#else
   float cwe[RPT], cwp[RPT];
 #pragma unroll
   for (int r = 0; r < RPT; ++r) {
@@ -158,7 +140,6 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
       wp2[r][k] = make_float2(wp[r][2 * k], wp[r][2 * k + 1]);
       we2[r][k] = make_float2(we[r][2 * k], we[r][2 * k + 1]);
     }
-#endif
   // the one (column, sample-in-block) item this lane finishes
   const int own = LR::own_base(lane);
   const int orow = own / kSB, osmp = own % kSB;
@@ -223,7 +204,6 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
           const float v8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
           for (int r = 0; r < RPT; ++r) {
-#if LTC_FWD_TANH
             // act = 0.5 + 0.5*tanh(z/2): the constant halves are folded into
             // cwe/cwp, the weights into the half-scale registers; synapses j and
             // j+1 run as one packed f32x2 lane pair.
@@ -236,15 +216,6 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
               sd2 = fma2(wp2[r][k], th, sd2);
             }
             const float sn_ = sn2.x + sn2.y, sd_ = sd2.x + sd2.y;
-#else
-            float sn_ = 0.f, sd_ = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float act = fwd_gate(j, sl[r][j], nm[r][j], v8[j]);
-              sn_ = fmaf(we[r][j], act, sn_);
-              sd_ = fmaf(wp[r][j], act, sd_);
-            }
-#endif
             acc[0][r * kSB + i] = sn_;
             acc[1][r * kSB + i] = sd_;
           }

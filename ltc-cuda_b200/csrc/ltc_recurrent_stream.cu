@@ -37,19 +37,6 @@ namespace ltc {
 // bounded waits of the streamed backward that expired (see ltc_cluster.cuh)
 __device__ int g_stream_wait_timeouts = 0;
 
-#ifdef LTC_STREAM_PROF
-// Phase profile of the streamed backward (variant builds only): SM cycles summed
-// over CTAs, measured by thread 0: [0] unfold start..first wait, [1] waits for
-// staged chunks (+ barrier), [2] chunk math, [3] post-loop barrier, [4] tails,
-// [5] cluster barrier, [6] unfolds, [7] issue of the next chunk's copies (inside [2]).
-__device__ unsigned long long g_stream_prof[8];
-#define LTC_PROF_T(v) const long long v = clock64()
-#define LTC_PROF_ADD(i, d) \
-  if (threadIdx.x == 0) atomicAdd(&g_stream_prof[i], (unsigned long long)(d))
-#else
-#define LTC_PROF_T(v)
-#define LTC_PROF_ADD(i, d)
-#endif
 
 namespace {
 
@@ -359,7 +346,6 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(const __grid_constant__
   const float2 m1 = make_float2(-1.f, -1.f);
   int t = T - 1, k = U - 1;
   for (int n = NTU - 1; n >= 0; --n) {
-    LTC_PROF_T(p_u0);
     for (int i = tid; i < ns * NEUR; i += kNT) DV[i] = 0.f;
     const float* VP = VPb + (n & 1) * ns * NEUR;       // V[n], staged one unfold ahead
     const float* VPm = VPb + ((n + 1) & 1) * ns * NEUR;  // V[n-1], staged now for the tails
@@ -368,18 +354,12 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(const __grid_constant__
       cp_async_commit();
     }
     stage(n, 0, 0);
-    LTC_PROF_T(p_u1);
-    LTC_PROF_ADD(0, p_u1 - p_u0);
     for (int c = 0; c < NC; ++c) {
-      LTC_PROF_T(p_c0);
       const int buf = c & 1;
       mbar_wait(smem_addr(&cbar[buf]), (cphase >> buf) & 1u, &cabort, &g_stream_wait_timeouts);
       cphase ^= 1u << buf;
       __syncthreads();  // everyone is past chunk c-1: its buffer takes chunk c+1
-      LTC_PROF_T(p_c1);
-      LTC_PROF_ADD(1, p_c1 - p_c0);
       if (c + 1 < NC) stage(n, c + 1, (c + 1) & 1);
-      LTC_PROF_ADD(7, clock64() - p_c1);
       float2 sl2[4], nm2[4], wp2[4], we2[4], G0[4], G1[4], G2[4], G3[4];
       // reordered chunk: synapse j of lane ql at j*QL + ql (2-way bank conflicts at most)
       const float4* pk = pks + buf * NEUR * QC + rl * QC + ql;
@@ -452,13 +432,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(const __grid_constant__
         *reinterpret_cast<float4*>(gdst + 2 * hp2 + 4 * h2) = make_float4(G2[k0].x, G2[k0].y, G2[k1].x, G2[k1].y);
         *reinterpret_cast<float4*>(gdst + 3 * hp2 + 4 * h2) = make_float4(G3[k0].x, G3[k0].y, G3[k1].x, G3[k1].y);
       }
-      LTC_PROF_ADD(2, clock64() - p_c1);
     }
-    LTC_PROF_T(p_t0);
     cp_async_wait_all();  // V[n-1] for the tails
     __syncthreads();
-    LTC_PROF_T(p_t1);
-    LTC_PROF_ADD(3, p_t1 - p_t0);
     // per-neuron tails of the own rows, samples s = ql + j*QL.  All global loads
     // of the thread's samples are issued first (the chunk registers are dead
     // here), then the math and stores run: the L2 latencies overlap instead of
@@ -518,13 +494,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_stream(const __grid_constant__
         }
       }
     }
-    LTC_PROF_T(p_s0);
-    LTC_PROF_ADD(4, p_s0 - p_t1);
     fence_proxy_async_global();  // slab write-back and a'_n/a'_d before the TMA reads
     cluster.sync();  // release a_n/a_d of unfold n-1 / acquire the peers'
-    LTC_PROF_T(p_s1);
-    LTC_PROF_ADD(5, p_s1 - p_s0);
-    LTC_PROF_ADD(6, p_s1 - p_u0);
     if (--k < 0) {
       k = U - 1;
       --t;
@@ -680,10 +651,5 @@ int read_stream_wait_timeouts(int* count) {
   return (int)cudaMemcpyFromSymbol(count, g_stream_wait_timeouts, sizeof(int));
 }
 
-#ifdef LTC_STREAM_PROF
-extern "C" int ltc_debug_stream_prof(unsigned long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, g_stream_prof, sizeof(g_stream_prof));
-}
-#endif
 
 }  // namespace ltc

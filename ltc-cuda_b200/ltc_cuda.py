@@ -216,6 +216,27 @@ def wait_timeouts() -> int:
     return n
 
 
+_CHECK_WAITS = [False, 0]
+
+
+def set_check_waits(on: bool) -> None:
+    """Opt-in health check: when on, every backward pass ends by reading the device's
+    expired-wait counter (one small device-to-host read, so it synchronises the device)
+    and raises ``RuntimeError`` if a bounded in-kernel wait expired since the previous
+    check -- such a launch finished without its peer data and its results are invalid.
+    Off by default; callers that leave it off should poll :func:`wait_timeouts` at a
+    step boundary they already synchronise on."""
+    _CHECK_WAITS[0] = bool(on)
+    _CHECK_WAITS[1] = wait_timeouts() if on else 0
+
+
+def _check_waits_after(where: str) -> None:
+    n = wait_timeouts()
+    if n != _CHECK_WAITS[1]:
+        _CHECK_WAITS[1] = n
+        raise RuntimeError(f"{where}: {n} bounded in-kernel wait(s) expired on this device; results are invalid")
+
+
 def _params_struct(ts: Sequence[torch.Tensor]) -> LtcParams:
     return LtcParams(*[t.data_ptr() for t in ts])
 
@@ -435,6 +456,8 @@ class LTCCudaForward(torch.autograd.Function):
         g = _cuda_module.ltc_full_backward(x_seq, state, w_pos, w_erev, mu, sigma, smu, ssig, serev, sw, cm_t,
                                            gleak_pos, vleak, buf, grad_outputs, grad_state, ctx.ode_unfolds,
                                            ctx.epsilon, grad_state is not None)
+        if _CHECK_WAITS[0]:
+            _check_waits_after("LTCCudaForward.backward")
         return (*g, None, None, None)
 
 

@@ -39,10 +39,12 @@ def rel_err(a, b):
     return ((a - b).abs().max() / b.abs().max().clamp_min(1e-12)).item()
 
 
-def oracle_solver(inp, U, eps, gout=None, gh=None, device="cpu", chunk=None, dtype=torch.float32):
-    """Oracle outputs and gradients (B-chunked for the larger workloads)."""
+def oracle_solver(inp, U, eps, gout=None, gh=None, device="cpu", chunk=None, dtype=torch.float32,
+                  checkpoint=False):
+    """Oracle outputs and gradients (B-chunked, optionally step-checkpointed, for the
+    larger workloads)."""
     moved = {k: v.detach().to(device) for k, v in inp.items()}
     return orc.function_grads(moved, U, eps,
                               grad_out=None if gout is None else gout.to(device),
                               grad_state=None if gh is None else gh.to(device),
-                              batch_chunk=chunk, dtype=dtype)
+                              batch_chunk=chunk, dtype=dtype, checkpoint=checkpoint)
