@@ -298,6 +298,13 @@ def module_parity(run_ours, make_ours, ltc, p, cfg, dev):
             "pass": bool(fwd < 1e-3 and ok), "against": "reference ltc.py TorchScript path on the GPU"}
 
 
+def rec_synapses(model, cfg) -> int:
+    """Recurrent synapses per unfold the kernels visit (see ltc_cuda.skip_zero_synapses)."""
+    if getattr(model, "skip_zero_synapses", False) and cfg.H <= 64:
+        return int(model.sparsity_mask.count_nonzero().item())
+    return cfg.H * cfg.H
+
+
 def our_parity(cfg, p, dev):
     """Parity of this build's module on a slice of the timed configuration, checked
     before the timed region against the reference TorchScript path (or, where the
@@ -551,8 +558,11 @@ def main():
     # ---- roofline of the dominant kernel (MUFU pipe: 2 MUFU ops per synapse visit) ----
     f_mhz = float(peaks.get("sm_max_mhz", 1965.0))
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    visits = {"recurrent_fwd": Bl * cfg.T * cfg.U * cfg.H * cfg.H,
-              "recurrent_bwd": Bl * cfg.T * cfg.U * cfg.H * cfg.H,
+    # recurrent synapses the kernels visit: the nonzero ones when the module lets the
+    # solver skip masked synapses (H <= 64), else all H*H
+    rec_syn = rec_synapses(model, cfg)
+    visits = {"recurrent_fwd": Bl * cfg.T * cfg.U * rec_syn,
+              "recurrent_bwd": Bl * cfg.T * cfg.U * rec_syn,
               "sensory_fwd": Bl * cfg.T * cfg.D * cfg.H,
               "sensory_bwd": Bl * cfg.T * cfg.D * cfg.H}
     # Work per step of each kernel kind.  Memory-lean training runs the forward
@@ -576,11 +586,11 @@ def main():
     kernels = {k: {"ms_total": round(v[0], 3), "launches": v[1], "share": round(v[0] / max(1e-9, sum(
         t for t, _ in ktimes.values())), 4)} for k, v in ktimes.items()}
     # whole-step ceiling with the survey's counting convention (4 MUFU per fwd+bwd synapse visit)
-    S = cfg.D * cfg.H + cfg.U * cfg.H * cfg.H
+    S = cfg.D * cfg.H + cfg.U * rec_syn  # nonzero recurrent synapses when they are skipped
     t_roof = cfg.B * cfg.T * S * 4 / (16 * sms * f_mhz * 1e6 * world)
     # recurrent kernels alone, same convention (the H=128 north-star figure)
     per_step = lambda k: ktimes[k][0] / args.steps / 1e3  # seconds of kernel kind k per step
-    t_roof_rec = Bl * cfg.T * cfg.U * cfg.H * cfg.H * 4 / (16 * sms * f_mhz * 1e6)
+    t_roof_rec = Bl * cfg.T * cfg.U * rec_syn * 4 / (16 * sms * f_mhz * 1e6)
     rec_frac = t_roof_rec / (per_step("recurrent_fwd") + per_step("recurrent_bwd"))
     # sensory forward: reads x (4 D B per (b,t)), writes sn/sd (8 H B); MUFU-bound, not HBM-bound
     sens_gbs = twice * Bl * cfg.T * (4 * cfg.D + 8 * cfg.H) / per_step("sensory_fwd") / 1e9
@@ -595,7 +605,8 @@ def main():
                    "parallelism": f"dp{world}", "per_rank_batch": Bl,
                    "l2": "256 MB flush write between steps (inside the timed region)",
                    "cuda_graph": use_graph if graph_note is None else graph_note,
-                   "saved_state": "step boundaries, unfolds recomputed (lean)" if args.lean else "every unfold"},
+                   "saved_state": "step boundaries, unfolds recomputed (lean)" if args.lean else "every unfold",
+                   "recurrent_synapses_visited": rec_syn, "recurrent_synapses_dense": cfg.H * cfg.H},
         "e2e": e2e,
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
                      "frac": achieved / peak, "ms_per_launch": ms_per_launch,

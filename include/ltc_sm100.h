@@ -43,6 +43,21 @@ typedef struct {
  * segment, newest first) with the forward kernels and accumulates the parameter
  * partials across segments.  Cost: one extra recurrent + sensory forward. */
 #define LTC_FLAG_LEAN_SAVE 2
+/* Skip structurally-zero recurrent synapses (no counterpart in the reference, whose
+ * kernels visit all H*H synapses, csrc/ltc_kernels.cu:115-192,549-668).  A synapse
+ * whose w_pos and w_erev are both zero adds nothing to the forward solve and has
+ * dL/dz = 0, so its only gradient terms are those of w_pos / w_erev at its own
+ * position.  With this flag the caller declares those entries unused -- true
+ * whenever w_pos = softplus(w) * mask, since the chain rule multiplies them by the
+ * mask -- and the solver visits only the nonzero synapses; the four recurrent
+ * gradients (w_pos, w_erev, mu, sigma) are written as zero at the skipped
+ * positions.  Every other output is unchanged.  Honoured for H <= 64 (other sizes
+ * run the dense kernels); the slot tables are rebuilt on the device at every call.
+ * Capacity: for 32 < H <= 64 every neuron may have at most 48 nonzero incoming and
+ * 48 nonzero outgoing synapses (any pattern fits for H <= 32).  The library cannot
+ * report a violation without a device sync, so a call that exceeds it writes NaN
+ * to its outputs and gradients; check the pattern before setting the flag. */
+#define LTC_FLAG_SKIP_ZERO_SYNAPSES 4
 /* Bits 8..23 of flags, if nonzero, fix the lean segment length in steps
  * (otherwise it is sized for about 512 MiB of per-unfold state). */
 #define LTC_LEAN_CHUNK_SHIFT 8

@@ -146,7 +146,8 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
   if (di->major != 10)
     return fail("libltc_sm100 requires an sm_100 (B200-class) GPU; current device is compute capability %d.x",
                 di->major);
-  L->rp = plan_recurrent(d->B, d->H, di->sms, d->flags & LTC_FLAG_FORCE_WIDE);
+  L->rp = plan_recurrent(d->B, d->H, di->sms, d->flags & LTC_FLAG_FORCE_WIDE,
+                         (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) != 0);
   L->rows = (long long)d->B * d->T;
   L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
   const size_t tu = (size_t)d->T * d->ode_unfolds;
@@ -176,6 +177,7 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
 struct FwdBuffers {
   float4 *pack, *spack, *nrn;
   float *sn, *sd, *scratch;
+  void* tables;  // sparse path only
 };
 size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
   Carver c(ws);
@@ -186,6 +188,7 @@ size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
   b->sn = c.take<float>((size_t)L.rows * d->H);
   b->sd = c.take<float>((size_t)L.rows * d->H);
   b->scratch = L.rp.scratch_fwd ? c.take<float>(L.rp.scratch_fwd) : nullptr;
+  b->tables = L.rp.sparse ? c.take<char>(sparse_tables_bytes(HP)) : nullptr;
   return c.off + 256;
 }
 
@@ -194,6 +197,7 @@ struct BwdBuffers {
   float *gsn, *gsd, *rpart, *rpartn, *spart, *dxpart, *scratch;
   // lean backward: one segment's staged inputs, recomputed state and outputs
   float *xc, *snc, *sdc, *gsnc, *gsdc, *Vc, *Rc, *hs, *ghA, *ghB, *fscratch;
+  void* tables;  // sparse path only
 };
 size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   Carver c(ws);
@@ -209,6 +213,7 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->spart = c.take<float>(L.sp.part_floats);
   b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
   b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
+  b->tables = L.rp.sparse ? c.take<char>(sparse_tables_bytes(HP)) : nullptr;
   b->xc = b->snc = b->sdc = b->gsnc = b->gsdc = b->Vc = b->Rc = b->hs = b->ghA = b->ghB = b->fscratch = nullptr;
   if (L.lean) {
     const size_t BH = (size_t)d->B * d->H, tcu = (size_t)L.tc * d->ode_unfolds;
@@ -401,6 +406,11 @@ int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, co
     e = launch_pack(pa, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "pack");
+  if (L.rp.sparse) {
+    TimedLaunch tl(LTC_KERNEL_PACK_FWD, st);
+    e = launch_build_slots(pa, b.tables, st);
+    if (e != cudaSuccess) return cuda_fail(e, "build_slots");
+  }
 
   SensFwdArgs sa{};
   sa.spack = b.spack; sa.x = x; sa.sn = b.sn; sa.sd = b.sd; sa.rows = L.rows;
@@ -420,7 +430,7 @@ int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, co
     ra.R = c.take<float>(L.saved_floats_r);
   }
   ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
-  ra.ns = L.rp.ns_fwd; ra.eps = dims->epsilon; ra.scratch = b.scratch;
+  ra.ns = L.rp.ns_fwd; ra.eps = dims->epsilon; ra.scratch = b.scratch; ra.tables = b.tables;
   {
     TimedLaunch tl(LTC_KERNEL_RECURRENT_FWD, st);
     e = launch_recurrent_fwd(ra, L.rp, st);
@@ -470,6 +480,11 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
     e = launch_pack(pa, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "pack");
+  if (L.rp.sparse) {
+    TimedLaunch tl(LTC_KERNEL_PACK_BWD, st);
+    e = launch_build_slots(pa, b.tables, st);
+    if (e != cudaSuccess) return cuda_fail(e, "build_slots");
+  }
 
   Carver sc(const_cast<void*>(saved));
   RecBwdArgs ra{};
@@ -478,7 +493,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   ra.gstate = grad_state; ra.gsn = b.gsn; ra.gsd = b.gsd; ra.gh0 = grads->state;
   ra.part = b.rpart; ra.partn = b.rpartn;
   ra.B = dims->B; ra.T = dims->T; ra.H = dims->H; ra.U = dims->ode_unfolds; ra.HP = HP;
-  ra.ns = L.rp.ns_bwd; ra.scratch = b.scratch;
+  ra.ns = L.rp.ns_bwd; ra.scratch = b.scratch; ra.tables = b.tables;
   if (!L.lean) {
     ra.V = sc.take<float>(L.saved_floats_v);
     ra.R = sc.take<float>(L.saved_floats_r);
@@ -503,6 +518,10 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   FinishArgs fa{};
   fa.rec_part = b.rpart; fa.rec_partn = b.rpartn; fa.rslots = L.rp.slots_bwd; fa.rec_transposed = L.rp.wide && !L.rp.streamed;
   fa.rec_tanh_space = L.rp.tanh_space;
+  if (L.rp.sparse) {
+    fa.skip_w_pos = params->w_pos;
+    fa.skip_w_erev = params->w_erev;
+  }
   fa.sens_part = b.spart; fa.nsplit = L.sp.nsplit; fa.dxpart = b.dxpart; fa.nqc = L.sp.nqc; fa.rows = L.rows;
   fa.mu = params->mu; fa.sigma = params->sigma; fa.smu = params->sensory_mu; fa.ssig = params->sensory_sigma;
   fa.serev = params->sensory_erev; fa.sw = params->sensory_w_pos;
@@ -561,7 +580,7 @@ int lean_recurrent_backward(const LtcDims* dims, const Layout& L, const DeviceIn
     fa.pack = b.pack; fa.nrn = b.nrn; fa.sn = b.snc; fa.sd = b.sdc; fa.h0 = h_start;
     fa.out = nullptr; fa.hT = nullptr; fa.V = b.Vc; fa.R = b.Rc;
     fa.B = B; fa.T = tc; fa.H = H; fa.U = dims->ode_unfolds; fa.HP = HP;
-    fa.ns = L.rp.ns_fwd; fa.eps = dims->epsilon; fa.scratch = b.fscratch;
+    fa.ns = L.rp.ns_fwd; fa.eps = dims->epsilon; fa.scratch = b.fscratch; fa.tables = b.tables;
     {
       TimedLaunch tl(LTC_KERNEL_RECURRENT_FWD, st);
       e = launch_recurrent_fwd(fa, L.rp, st);

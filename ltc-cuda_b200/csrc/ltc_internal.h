@@ -84,6 +84,7 @@ struct RecFwdArgs {
   int ns;               // samples per CTA
   float eps;
   float* scratch;       // plan.scratch_fwd floats (streamed path)
+  const void* tables;   // slot tables (sparse path, launch_build_slots)
 };
 struct RecBwdArgs {
   const float4* pack;   // [HP][HP] (fast path)
@@ -103,11 +104,13 @@ struct RecBwdArgs {
   int ns;
   float* scratch;       // plan.scratch_bwd floats (streamed path)
   int accumulate;       // add to part/partn (segments of a lean backward) instead of overwriting
+  const void* tables;   // slot tables (sparse path, launch_build_slots)
 };
 struct RecPlan {
   bool wide;       // not the register-resident kernels (streamed or generic wide-H)
   bool streamed;   // cluster-streamed kernels (128 < H <= 512)
   bool tanh_space; // synapse partials hold sum a'*tanh (a' = -a/4); partn has 5 rows (+ sum a_n, sum a_d)
+  bool sparse;     // zero synapses skipped (LTC_FLAG_SKIP_ZERO_SYNAPSES, H <= 64): slot-table kernels
   size_t scratch_fwd, scratch_bwd;  // floats of path-specific global scratch
   int HP;          // padded neuron count
   int ns_fwd, grid_fwd, threads_fwd;
@@ -115,7 +118,15 @@ struct RecPlan {
   int ns_bwd, grid_bwd, threads_bwd, slots_bwd;
   size_t smem_bwd;
 };
-RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide);
+// skip_zero: the caller set LTC_FLAG_SKIP_ZERO_SYNAPSES (honoured for H <= 64 without force_wide)
+RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide, bool skip_zero = false);
+// sparse path (ltc_recurrent_sparse.cu): slot tables built on the device from the
+// recurrent parameters (sparse_tables_bytes(HP) of workspace), then the kernels
+size_t sparse_tables_bytes(int HP);
+void plan_sparse(RecPlan& p, int B, int num_sms);
+cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st);
+cudaError_t launch_sparse_fwd(const RecFwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st);
+cudaError_t launch_sparse_bwd(const RecBwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st);
 // chunk width of the streamed backward (256 threads, 8-CTA clusters), 0 on other paths
 inline int stream_chunk_cols(const RecPlan& p) { return p.streamed ? 16384 / p.HP : 0; }
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);
@@ -131,6 +142,9 @@ struct FinishArgs {
   int rslots;
   bool rec_transposed;     // partial layout [q][p]
   bool rec_tanh_space;     // S0/S1 are sums of a'*tanh (a' = -a/4), partn rows 3/4 = sums of a_n/a_d
+  // sparse path: synapses with w_pos == w_erev == 0 were skipped; their four
+  // gradients are written as zero (their partial-slab entries are never written)
+  const float* skip_w_pos; const float* skip_w_erev;
   const float* sens_part;  // [nsplit][4][D*HP]
   int nsplit;
   const float* dxpart;     // [nqc][rows*D] or null

@@ -87,6 +87,10 @@ __global__ void finish_kernel(FinishArgs a) {
        i += (long long)gridDim.x * blockDim.x) {
     if (i < nrec) {
       const int p = (int)(i / a.H), q = (int)(i % a.H);
+      if (a.skip_w_pos && a.skip_w_pos[i] == 0.f && a.skip_w_erev[i] == 0.f) {
+        a.g_w_erev[i] = a.g_w_pos[i] = a.g_mu[i] = a.g_sigma[i] = 0.f;
+        continue;
+      }
       const long long idx = a.rec_transposed ? (long long)q * a.HP + p : (long long)p * a.HP + q;
       float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
       for (int c = 0; c < a.rslots; ++c) {

@@ -657,9 +657,13 @@ int resident_clusters(int CL, int num_sms) {
   return cache[dev][slot];
 }
 
-RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
+RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide, bool skip_zero) {
   RecPlan p{};
   p.HP = pad_neurons(H);
+  if (skip_zero && !force_wide && p.HP <= 64) {
+    plan_sparse(p, B, num_sms);
+    return p;
+  }
   if (force_wide) {
     p.wide = true;
     plan_wide(p, B, H, num_sms);
@@ -706,6 +710,7 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide) {
 }
 
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  if (p.sparse) return launch_sparse_fwd(a, p, a.tables, st);
   if (p.streamed) return launch_stream_fwd(a, p, st);
   if (p.wide) return launch_wide_fwd(a, p, st);
   switch (p.HP) {
@@ -716,6 +721,7 @@ cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStre
 }
 
 cudaError_t launch_recurrent_bwd(const RecBwdArgs& a, const RecPlan& p, cudaStream_t st) {
+  if (p.sparse) return launch_sparse_bwd(a, p, a.tables, st);
   if (p.streamed) return launch_stream_bwd(a, p, st);
   if (p.wide) return launch_wide_bwd(a, p, st);
   switch (p.HP) {

@@ -1,0 +1,734 @@
+// Recurrent kernels that skip structurally-zero synapses (H <= 64, LTC_FLAG_SKIP_ZERO_SYNAPSES).
+//
+// A synapse whose w_pos and w_erev are both zero adds nothing to the solve
+// (num/den terms are w * act) and has dL/dz = 0, so it only contributes to the
+// gradients of w_pos / w_erev at its own position -- which a module that builds
+// w_pos = softplus(w) * mask multiplies by zero.  With the flag the caller
+// declares those gradients unused; these kernels then visit only the nonzero
+// synapses and the finish kernel writes zeros at the skipped positions.
+//
+// Layout.  8 lanes share a PAIR of neurons (rows in the backward, columns in the
+// forward): the c-th heaviest and the c-th lightest by nonzero count, so every
+// pair carries a similar total.  Each lane holds up to KM synapses of each
+// neuron, taken from the neuron's nonzero list (entry e -> lane e % 8, slot
+// e / 8); a warp (4 pairs) runs its slot counts (K1, K2) -- the largest of its
+// heavy / light neurons' ceil(count / 8) -- as compile-time constants, chosen by
+// a switch at the top of each sample block, so no per-slot branch is issued.
+// The per-neuron vectors the synapse pass gathers from (v in the forward, the
+// adjoints in the backward) are stored neuron-major, four samples per float4,
+// with an odd number of float4 per neuron; lists are ordered round-robin over the
+// residue mod 8, so the eight lanes of a quarter-warp (one pair) gather from
+// distinct bank groups.  The packed f32x2 pairs run over two SAMPLES of one
+// synapse (adjacent in the gathered float4), with the synapse constants
+// duplicated in both halves, so forming the pairs costs no register moves.
+//
+// Capacity: KM slots per neuron and lane (HP = 64: 6, i.e. at most 48 nonzero
+// synapses per neuron; HP = 32: 4, any mask).  The table builder checks it; a
+// call whose mask exceeds it writes NaN to every output of the kernels (state,
+// outputs, gradients) instead of a wrong number -- callers check the mask first
+// (ltc_cuda.skip_zero_synapses does).
+//
+// Tables are rebuilt on the device at every call (build_slots_kernel, one CTA),
+// so the host never reads the mask and CUDA-graph capture stays possible.
+#include <cstdint>
+#include <type_traits>
+
+#include "ltc_common.cuh"
+#include "ltc_internal.h"
+
+namespace ltc {
+namespace {
+
+constexpr int kSB = 4;   // samples per block (one float4 of a neuron-major vector)
+constexpr int kTPC = 8;  // lanes per neuron pair
+template <int HP>
+constexpr int slots_max() { return HP == 64 ? 6 : 4; }
+
+// slot tables inside the caller's workspace (see sparse_tables_bytes)
+struct SlotTablesView {
+  int* fneu;      // [HP]          neuron of (pair c, r) at 2c + r (forward: column q)
+  int* fk;        // [warps]       K1 | K2 << 8
+  float4* fpack;  // [NT][2][KM]   (sigma/2, -sigma*mu/2, w_pos/2, w_erev/2)
+  int* fidx;      // [NT][2][KM]   presynaptic neuron p, -1 = padding
+  int* bneu;      // [HP]          backward: row p
+  int* bk;        // [warps]
+  float4* bpack;  // [NT][2][KM]   (-sigma/2, sigma*mu/2, w_pos, w_erev)
+  int* bidx;      // [NT][2][KM]   postsynaptic neuron q, -1 = padding
+  int* overflow;  // [1]           1 if a neuron has more than 8 * KM nonzero synapses
+};
+
+__host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+// byte offsets of the table arrays; returns the total size
+inline size_t tables_layout(int HP, size_t (&at)[9]) {
+  const int NT = 4 * HP, KM = HP == 64 ? 6 : 4, NW = NT / 32;
+  const size_t sz[9] = {HP * sizeof(int), NW * sizeof(int), (size_t)NT * 2 * KM * sizeof(float4),
+                        (size_t)NT * 2 * KM * sizeof(int), HP * sizeof(int), NW * sizeof(int),
+                        (size_t)NT * 2 * KM * sizeof(float4), (size_t)NT * 2 * KM * sizeof(int), sizeof(int)};
+  size_t o = 0;
+  for (int i = 0; i < 9; ++i) {
+    at[i] = o;
+    o = align_up(o + sz[i]);
+  }
+  return o;
+}
+
+inline SlotTablesView tables_view(void* base, int HP) {
+  char* b = static_cast<char*>(base);
+  size_t at[9];
+  tables_layout(HP, at);
+  SlotTablesView v;
+  v.fneu = reinterpret_cast<int*>(b + at[0]);
+  v.fk = reinterpret_cast<int*>(b + at[1]);
+  v.fpack = reinterpret_cast<float4*>(b + at[2]);
+  v.fidx = reinterpret_cast<int*>(b + at[3]);
+  v.bneu = reinterpret_cast<int*>(b + at[4]);
+  v.bk = reinterpret_cast<int*>(b + at[5]);
+  v.bpack = reinterpret_cast<float4*>(b + at[6]);
+  v.bidx = reinterpret_cast<int*>(b + at[7]);
+  v.overflow = reinterpret_cast<int*>(b + at[8]);
+  return v;
+}
+
+// ---- table builder: one CTA of 256 threads ---------------------------------
+// Backward: neuron = row p, list = its nonzero columns q.  Forward: neuron =
+// column q, list = its nonzero rows p.
+template <int HP>
+__global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, const float* __restrict__ w_pos,
+                                                          const float* __restrict__ w_erev,
+                                                          const float* __restrict__ sigma,
+                                                          const float* __restrict__ mu, int H) {
+  constexpr int KM = slots_max<HP>(), NPAIR = HP / 2, PPW = 32 / kTPC;  // pairs per warp
+  __shared__ uint64_t nz[2][HP];  // [0] bit q of row p; [1] bit p of column q
+  __shared__ int cnt[2][HP];
+  __shared__ int order[2][HP];    // neurons by count, descending
+  const int tid = threadIdx.x;
+  for (int p = tid; p < HP; p += blockDim.x) {
+    uint64_t m = 0;
+    if (p < H)
+      for (int q = 0; q < H; ++q) {
+        const long long j = (long long)p * H + q;
+        if (w_pos[j] != 0.f || w_erev[j] != 0.f) m |= 1ull << q;
+      }
+    nz[0][p] = m;
+    cnt[0][p] = __popcll(m);
+  }
+  __syncthreads();
+  for (int q = tid; q < HP; q += blockDim.x) {
+    uint64_t m = 0;
+    for (int p = 0; p < HP; ++p)
+      if ((nz[0][p] >> q) & 1ull) m |= 1ull << p;
+    nz[1][q] = m;
+    cnt[1][q] = __popcll(m);
+  }
+  __syncthreads();
+  for (int i = tid; i < 2 * HP; i += blockDim.x) {  // stable rank by count, descending
+    const int s = i / HP, n = i % HP, c = cnt[s][n];
+    int r = 0;
+    for (int m = 0; m < HP; ++m) r += (cnt[s][m] > c) || (cnt[s][m] == c && m < n);
+    order[s][r] = n;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int over = 0;
+    for (int i = 0; i < 2 * HP; ++i) over |= cnt[i / HP][i % HP] > kTPC * KM;
+    *tv.overflow = over;
+  }
+  // neuron of (pair c, r): r = 0 the c-th heaviest, r = 1 the c-th lightest
+  for (int i = tid; i < 2 * HP; i += blockDim.x) {
+    const int s = i / HP, k = i % HP, c = k / 2, r = k % 2;
+    (s ? tv.fneu : tv.bneu)[k] = order[s][r ? HP - 1 - c : c];
+  }
+  for (int i = tid; i < 2 * (NPAIR / PPW); i += blockDim.x) {  // slot counts per warp
+    const int s = i / (NPAIR / PPW), w = i % (NPAIR / PPW);
+    int k1 = 0, k2 = 0;
+    for (int c = PPW * w; c < PPW * w + PPW; ++c) {
+      k1 = max(k1, min(KM, (cnt[s][order[s][c]] + kTPC - 1) / kTPC));
+      k2 = max(k2, min(KM, (cnt[s][order[s][HP - 1 - c]] + kTPC - 1) / kTPC));
+    }
+    (s ? tv.fk : tv.bk)[w] = k1 | (k2 << 8);
+  }
+  // lists: one thread per (side, pair, r); entries round-robin over residues mod 8
+  for (int i = tid; i < 2 * HP; i += blockDim.x) {
+    const int s = i / HP, k = i % HP, c = k / 2, r = k % 2;
+    const int n = order[s][r ? HP - 1 - c : c];
+    const uint64_t m = nz[s][n];
+    float4* pk = s ? tv.fpack : tv.bpack;
+    int* ix = s ? tv.fidx : tv.bidx;
+    int next[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) next[b] = b;
+    int e = 0;
+    const int total = min(__popcll(m), kTPC * KM);
+    while (e < total) {
+      for (int b = 0; b < 8 && e < total; ++b) {
+        int o = next[b];
+        while (o < HP && !((m >> o) & 1ull)) o += 8;
+        if (o >= HP) continue;
+        next[b] = o + 8;
+        const int p = s ? o : n, q = s ? n : o;  // synapse (p, q)
+        const long long j = (long long)p * H + q;
+        const float sg = sigma[j], wp = w_pos[j], we = w_erev[j];
+        const int slot = ((c * kTPC + e % kTPC) * 2 + r) * KM + e / kTPC;
+        pk[slot] = s ? make_float4(0.5f * sg, -0.5f * sg * mu[j], 0.5f * wp, 0.5f * we)
+                     : make_float4(-0.5f * sg, 0.5f * sg * mu[j], wp, we);
+        ix[slot] = o;
+        ++e;
+      }
+    }
+    for (; e < kTPC * KM; ++e) {
+      const int slot = ((c * kTPC + e % kTPC) * 2 + r) * KM + e / kTPC;
+      pk[slot] = make_float4(0.f, 0.f, 0.f, 0.f);
+      ix[slot] = -1;
+    }
+  }
+}
+
+// float4 stride (in float4 units) of a neuron's per-sample vector: odd, >= ns/4
+__host__ __device__ inline int neuron_stride4(int ns) {
+  const int s4 = (ns + 3) / 4;
+  return (s4 & 1) ? s4 : s4 + 1;
+}
+
+// the warp's (K1, K2) -> the compile-time pass (K1 >= K2, both <= KM): one jump
+// table (kw = K1 | K2 << 8), not a chain of compares
+template <int KM, typename Fn>
+__device__ __forceinline__ void dispatch_kk(int kw, Fn&& fn) {
+  using I0 = std::integral_constant<int, 0>;
+  switch (kw) {
+    case 0: fn(I0{}, I0{}); return;
+    case 1: fn(std::integral_constant<int, 1>{}, I0{}); return;
+    case 1 | (1 << 8): fn(std::integral_constant<int, 1>{}, std::integral_constant<int, 1>{}); return;
+    case 2: fn(std::integral_constant<int, 2>{}, I0{}); return;
+    case 2 | (1 << 8): fn(std::integral_constant<int, 2>{}, std::integral_constant<int, 1>{}); return;
+    case 2 | (2 << 8): fn(std::integral_constant<int, 2>{}, std::integral_constant<int, 2>{}); return;
+    case 3: fn(std::integral_constant<int, 3>{}, I0{}); return;
+    case 3 | (1 << 8): fn(std::integral_constant<int, 3>{}, std::integral_constant<int, 1>{}); return;
+    case 3 | (2 << 8): fn(std::integral_constant<int, 3>{}, std::integral_constant<int, 2>{}); return;
+    case 3 | (3 << 8): fn(std::integral_constant<int, 3>{}, std::integral_constant<int, 3>{}); return;
+    case 4: fn(std::integral_constant<int, 4>{}, I0{}); return;
+    case 4 | (1 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 1>{}); return;
+    case 4 | (2 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 2>{}); return;
+    case 4 | (3 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 3>{}); return;
+    default: break;
+  }
+  if constexpr (KM >= 6) {
+    switch (kw) {
+      case 4 | (4 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 4>{}); return;
+      case 5: fn(std::integral_constant<int, 5>{}, I0{}); return;
+      case 5 | (1 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 1>{}); return;
+      case 5 | (2 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 2>{}); return;
+      case 5 | (3 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 3>{}); return;
+      case 5 | (4 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 4>{}); return;
+      case 5 | (5 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 5>{}); return;
+      case 6: fn(std::integral_constant<int, 6>{}, I0{}); return;
+      case 6 | (1 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 1>{}); return;
+      case 6 | (2 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 2>{}); return;
+      case 6 | (3 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 3>{}); return;
+      case 6 | (4 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 4>{}); return;
+      case 6 | (5 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 5>{}); return;
+      default: fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 6>{}); return;
+    }
+  } else {
+    fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 4>{});
+  }
+}
+
+// 16-bit byte offsets of a lane's slots (two per register)
+template <int N>
+struct Offsets {
+  uint32_t w[(N + 1) / 2];
+  __device__ __forceinline__ void set(int j, uint32_t o) {
+    w[j / 2] = (j & 1) ? (w[j / 2] | (o << 16)) : o;
+  }
+  __device__ __forceinline__ uint32_t get(int j) const { return (j & 1) ? (w[j / 2] >> 16) : (w[j / 2] & 0xFFFFu); }
+};
+
+// ---- forward ------------------------------------------------------------------
+// vbuf[2][HP][S] neuron-major states (S = 4 * neuron_stride4(ns)); snb/sdb [ns][LDV].
+template <int HP>
+struct SparseFwd {
+  static constexpr int KM = slots_max<HP>(), NT = 4 * HP, LDV = HP + 4;
+  float2 sl2[2][KM], nm2[2][KM], wp2[2][KM], we2[2][KM];  // duplicated constants
+  Offsets<2 * KM> off;
+  float cwe[2], cwp[2];
+
+  template <int R, int K>
+  __device__ __forceinline__ void row(const char* vb, float2 (&sn2)[2], float2 (&sd2)[2]) const {
+    sn2[0] = sn2[1] = make_float2(cwe[R], cwe[R]);
+    sd2[0] = sd2[1] = make_float2(cwp[R], cwp[R]);
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(vb + off.get(R * KM + j));
+      const float2 th0 = tanh2(fma2(sl2[R][j], make_float2(v.x, v.y), nm2[R][j]));
+      const float2 th1 = tanh2(fma2(sl2[R][j], make_float2(v.z, v.w), nm2[R][j]));
+      sn2[0] = fma2(we2[R][j], th0, sn2[0]);
+      sd2[0] = fma2(wp2[R][j], th0, sd2[0]);
+      sn2[1] = fma2(we2[R][j], th1, sn2[1]);
+      sd2[1] = fma2(wp2[R][j], th1, sd2[1]);
+    }
+  }
+
+  // one block of 4 samples (vb = the block's first float4 in neuron 0's vector):
+  // acc[0] = sum w_erev act, acc[1] = sum w_pos act per (r, i); the constant
+  // halves of act = 1/2 + tanh/2 are in cwe/cwp, as in the dense kernel
+  template <int K1, int K2>
+  __device__ __forceinline__ void pass(const char* vb, float (&acc)[2][2 * kSB]) const {
+    float2 sn2[2][2], sd2[2][2];
+    row<0, K1>(vb, sn2[0], sd2[0]);
+    row<1, K2>(vb, sn2[1], sd2[1]);
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        acc[0][r * kSB + 2 * h] = sn2[r][h].x;
+        acc[0][r * kSB + 2 * h + 1] = sn2[r][h].y;
+        acc[1][r * kSB + 2 * h] = sd2[r][h].x;
+        acc[1][r * kSB + 2 * h + 1] = sd2[r][h].y;
+      }
+  }
+};
+
+template <int HP>
+__global__ void __launch_bounds__(4 * HP, 1) rec_fwd_sparse(RecFwdArgs a, SlotTablesView tv) {
+  using F = SparseFwd<HP>;
+  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV;
+  using LR = LaneReduce<kTPC, 2 * kSB>;
+  extern __shared__ __align__(16) float smem[];
+  const int ns = a.ns;
+  const int S = 4 * neuron_stride4(ns);
+  float* vbuf = smem;                 // [2][HP][S]
+  float* snb = vbuf + 2 * HP * S;     // [ns][LDV]
+  float* sdb = snb + ns * LDV;        // [ns][LDV]
+
+  const int tid = threadIdx.x, lane = tid & 31, c = tid / kTPC;
+  const int H = a.H, B = a.B, T = a.T, U = a.U;
+  const int b0 = blockIdx.x * ns;
+  const int nvalid = min(ns, B - b0);
+  const int nblk = (nvalid + kSB - 1) / kSB;
+  const int kw = tv.fk[tid / 32];
+  const bool overflow = *tv.overflow != 0;
+
+  F f;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    f.cwe[r] = f.cwp[r] = 0.f;
+#pragma unroll
+    for (int j = 0; j < KM; ++j) {
+      const int base = (tid * 2 + r) * KM + j;
+      const float4 pk = tv.fpack[base];
+      const int ix = tv.fidx[base];
+      f.sl2[r][j] = make_float2(pk.x, pk.x);
+      f.nm2[r][j] = make_float2(pk.y, pk.y);
+      f.wp2[r][j] = make_float2(pk.z, pk.z);
+      f.we2[r][j] = make_float2(pk.w, pk.w);
+      f.cwe[r] += pk.w;
+      f.cwp[r] += pk.z;
+      f.off.set(r * KM + j, (uint32_t)((ix < 0 ? 0 : ix) * S * 4));
+    }
+  }
+  const int own = LR::own_base(lane);
+  const int orow = own / kSB, osmp = own % kSB;
+  const int q = tv.fneu[2 * c + orow];
+  const float4 nq = a.nrn[q];
+  const float cm = nq.x, cmgl = nq.x + nq.y, glvl = nq.w;
+  const bool qvalid = q < H;
+  const bool writer = LR::writer(lane);
+
+  for (int i = tid; i < 2 * HP * S + 2 * ns * LDV; i += NT) smem[i] = 0.f;
+  __syncthreads();
+  if (a.h0) {
+    for (int i = tid; i < nvalid * H; i += NT) {
+      const int s = i / H, h = i % H;
+      vbuf[h * S + s] = a.h0[(long long)(b0 + s) * H + h];
+    }
+  }
+  int cur = 0;
+  for (int t = 0; t < T; ++t) {
+    __syncthreads();
+    for (int i = tid; i < nvalid * H; i += NT) {
+      const int s = i / H, h = i % H;
+      const long long row = (long long)(b0 + s) * T + t;
+      snb[s * LDV + h] = a.sn[row * H + h];
+      sdb[s * LDV + h] = a.sd[row * H + h];
+    }
+    __syncthreads();
+    for (int u = 0; u < U; ++u) {
+      const long long n = (long long)t * U + u;
+      const float* __restrict__ vc = vbuf + cur * HP * S;
+      float* __restrict__ vn = vbuf + (cur ^ 1) * HP * S;
+      for (int blk = 0; blk < nblk; ++blk) {
+        float acc[2][2 * kSB];
+        const char* vb = reinterpret_cast<const char*>(vc) + 16 * blk;
+        dispatch_kk<KM>(kw, [&](auto K1, auto K2) {
+          f.template pass<decltype(K1)::value, decltype(K2)::value>(vb, acc);
+        });
+        LR::template run<2>(acc, lane);
+        const int s = blk * kSB + osmp;
+        const float v = vc[q * S + s];
+        const float wn = acc[0][0] + snb[s * LDV + q];
+        const float wd = acc[1][0] + sdb[s * LDV + q];
+        const float num = (cm * v + glvl) + wn;
+        const float rr = rcp_approx((cmgl + wd) + a.eps);
+        const float vnew = overflow ? __int_as_float(0x7fc00000) : num * rr;
+        if (writer && qvalid && s < nvalid) {
+          vn[q * S + s] = vnew;
+          const long long bs = b0 + s;
+          if (a.V) {
+            a.V[(n * B + bs) * H + q] = v;
+            a.R[(n * B + bs) * H + q] = rr;
+          }
+          if (u == U - 1 && a.out) a.out[(bs * T + t) * H + q] = vnew;
+        }
+      }
+      __syncthreads();
+      cur ^= 1;
+    }
+  }
+  const float* vc = vbuf + cur * HP * S;
+  for (int i = tid; i < nvalid * H; i += NT) {
+    const int s = i / H, h = i % H;
+    const long long bs = b0 + s;
+    if (a.hT) a.hT[bs * H + h] = vc[h * S + s];
+    if (a.V) a.V[((long long)T * U * B + bs) * H + h] = vc[h * S + s];
+  }
+}
+
+// ---- backward -----------------------------------------------------------------
+// AN/AD[2][HP][S] neuron-major adjoints (tanh space, a' = -a/4) of the unfold being
+// processed and the next one; VS[3], RS[2], DIR, GSN, GSD [ns][LDV] as in the dense kernel.
+template <int HP>
+struct SparseBwd {
+  static constexpr int KM = slots_max<HP>(), NT = 4 * HP, LDV = HP + 4;
+  float2 sl2[2][KM], nm2[2][KM], wp2[2][KM], we2[2][KM];   // duplicated constants
+  float2 Gwe[2][KM], Gwp[2][KM], Gdz[2][KM], Gdzv[2][KM];  // (even, odd) sample sums
+  Offsets<2 * KM> off;
+
+  // neuron R's K slots over one block; dv[h] = sum of dL/dz * (-sigma/2) for samples (2h, 2h+1)
+  template <int R, int K>
+  __device__ __forceinline__ void row(const char* an_b, const char* ad_b, const float4& vr, float2 (&dv)[2]) {
+    const float2 m1 = make_float2(-1.f, -1.f);
+    const float2 vp[2] = {make_float2(vr.x, vr.y), make_float2(vr.z, vr.w)};
+    dv[0] = dv[1] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const uint32_t o = off.get(R * KM + j);
+      const float4 a4 = *reinterpret_cast<const float4*>(an_b + o);
+      const float4 d4 = *reinterpret_cast<const float4*>(ad_b + o);
+      const float2 an[2] = {make_float2(a4.x, a4.y), make_float2(a4.z, a4.w)};
+      const float2 ad[2] = {make_float2(d4.x, d4.y), make_float2(d4.z, d4.w)};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        // tanh space, as in the dense kernel: tn = tanh(-z/2), a' = -a/4
+        const float2 tn = tanh2(fma2(sl2[R][j], vp[h], nm2[R][j]));
+        const float2 dz = mul2(fma2(an[h], we2[R][j], mul2(ad[h], wp2[R][j])), fma2(tn, tn, m1));
+        Gwe[R][j] = fma2(an[h], tn, Gwe[R][j]);
+        Gwp[R][j] = fma2(ad[h], tn, Gwp[R][j]);
+        Gdz[R][j] = add2(Gdz[R][j], dz);
+        Gdzv[R][j] = fma2(dz, vp[h], Gdzv[R][j]);
+        dv[h] = fma2(dz, sl2[R][j], dv[h]);
+      }
+    }
+  }
+
+  template <int K1, int K2>
+  __device__ __forceinline__ void pass(const char* an_b, const char* ad_b, const float4 (&vr)[2],
+                                       float (&acc)[1][2 * kSB]) {
+    float2 dv[2][2];
+    row<0, K1>(an_b, ad_b, vr[0], dv[0]);
+    row<1, K2>(an_b, ad_b, vr[1], dv[1]);
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        acc[0][r * kSB + 2 * h] = dv[r][h].x;
+        acc[0][r * kSB + 2 * h + 1] = dv[r][h].y;
+      }
+  }
+};
+
+template <int HP>
+__global__ void __launch_bounds__(4 * HP, 1) rec_bwd_sparse(RecBwdArgs a, SlotTablesView tv) {
+  using F = SparseBwd<HP>;
+  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV;
+  using LR = LaneReduce<kTPC, 2 * kSB>;
+  extern __shared__ __align__(16) float smem[];
+  const int ns = a.ns;
+  const int S = 4 * neuron_stride4(ns);
+  const int SL = ns * LDV;
+  const int SA = HP * S;        // one neuron-major adjoint slab
+  float* AN = smem;             // [2][SA]
+  float* AD = AN + 2 * SA;      // [2][SA]
+  float* VS = AD + 2 * SA;      // [3][SL]
+  float* RS = VS + 3 * SL;      // [2][SL]
+  float* DIR = RS + 2 * SL;
+  float* GSN = DIR + SL;
+  float* GSD = GSN + SL;
+  float* red = GSD + SL;        // [5][HP][kTPC]
+
+  const int tid = threadIdx.x, lane = tid & 31, c = tid / kTPC, g = tid % kTPC;
+  const int H = a.H, B = a.B, T = a.T, U = a.U;
+  const int grp = blockIdx.x;
+  const int b0 = grp * ns;
+  const int nvalid = min(ns, B - b0);
+  const int nblk = (nvalid + kSB - 1) / kSB;
+  const int NTU = T * U;
+  const int kw = tv.bk[tid / 32];
+  const float bad = *tv.overflow ? __int_as_float(0x7fc00000) : 0.f;  // NaN poisons every output
+  const int rowA = tv.bneu[2 * c], rowB = tv.bneu[2 * c + 1];
+
+  F f;
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int j = 0; j < KM; ++j) {
+      const int base = (tid * 2 + r) * KM + j;
+      const float4 pk = tv.bpack[base];
+      const int ix = tv.bidx[base];
+      f.sl2[r][j] = make_float2(pk.x, pk.x);
+      f.nm2[r][j] = make_float2(pk.y, pk.y);
+      f.wp2[r][j] = make_float2(pk.z, pk.z);
+      f.we2[r][j] = make_float2(pk.w, pk.w);
+      f.Gwe[r][j] = f.Gwp[r][j] = f.Gdz[r][j] = f.Gdzv[r][j] = make_float2(bad, bad);
+      f.off.set(r * KM + j, (uint32_t)((ix < 0 ? 0 : ix) * S * 4));
+    }
+  const int own = LR::own_base(lane);
+  const int orow = own / kSB, osmp = own % kSB;
+  const int p = orow ? rowB : rowA;
+  const float4 np_ = a.nrn[p];
+  const float cm = np_.x, gl = np_.y, vl = np_.z;
+  const bool pvalid = p < H;
+  const bool writer = LR::writer(lane);
+  float gcm = bad, ggl = bad, gvl = bad, san = bad, sad = bad;
+
+  for (int i = tid; i < 4 * SA + 8 * SL; i += NT) smem[i] = 0.f;
+  __syncthreads();
+
+  auto stage_v = [&](int m) {
+    float* dst = VS + (m % 3) * SL;
+    const float* src = a.V + ((long long)m * B + b0) * H;
+    for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
+  };
+  auto stage_r = [&](int m) {
+    float* dst = RS + (m % 2) * SL;
+    const float* src = a.R + ((long long)m * B + b0) * H;
+    for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
+  };
+  stage_v(NTU);
+  stage_v(NTU - 1);
+  stage_r(NTU - 1);
+  if (NTU >= 2) {
+    stage_v(NTU - 2);
+    stage_r(NTU - 2);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+
+  // per-neuron prep of unfold m for (sample s, neuron p), as in the dense kernel;
+  // the adjoints go to the neuron-major slabs the synapse pass gathers from
+  auto prep = [&](const float* rs, const float* vin_s, const float* vout_s, float* an_d, float* ad_d, int s,
+                  float gval, bool first_of_step) {
+    const int idx = s * LDV + p;
+    const float r = rs[idx];
+    const float vin = vin_s[idx];
+    const float vout = vout_s[idx];
+    const float an = gval * r;
+    const float ad = -an * vout;
+    gcm = fmaf(an, vin - vout, gcm);
+    ggl = fmaf(an, vl - vout, ggl);
+    gvl = fmaf(an, gl, gvl);
+    san += an;
+    sad += ad;
+    GSN[idx] = first_of_step ? an : GSN[idx] + an;
+    GSD[idx] = first_of_step ? ad : GSD[idx] + ad;
+    DIR[idx] = an * cm;
+    an_d[p * S + s] = -0.25f * an;
+    ad_d[p * S + s] = -0.25f * ad;
+  };
+
+  if (writer && pvalid) {
+    const int m = NTU - 1;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int s = blk * kSB + osmp;
+      if (s < nvalid) {
+        const long long bs = b0 + s;
+        float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh] + bad;
+        if (a.gstate) gval += a.gstate[bs * H + p];
+        prep(RS + (m % 2) * SL, VS + (m % 3) * SL, VS + ((m + 1) % 3) * SL, AN + (m % 2) * SA,
+             AD + (m % 2) * SA, s, gval, true);
+      }
+    }
+  }
+  __syncthreads();
+
+  int t = T - 1, k = U - 1;
+  for (int n = NTU - 1; n >= 0; --n) {
+    if (n >= 2) {
+      stage_v(n - 2);
+      stage_r(n - 2);
+    }
+    cp_async_commit();
+    const int c2 = n % 2, c2m = c2 ^ 1;
+    const int c3 = n % 3, c3m = (n + 2) % 3;
+    const char* an_s = reinterpret_cast<const char*>(AN + c2 * SA);
+    const char* ad_s = reinterpret_cast<const char*>(AD + c2 * SA);
+    const float* vsn = VS + c3 * SL;
+    const float* vsm = VS + c3m * SL;
+    const float* rsm = RS + c2m * SL;
+    float* an_m = AN + c2m * SA;
+    float* ad_m = AD + c2m * SA;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const float* vb = vsn + blk * kSB * LDV;
+      const float4 vr[2] = {make_float4(vb[rowA], vb[LDV + rowA], vb[2 * LDV + rowA], vb[3 * LDV + rowA]),
+                            make_float4(vb[rowB], vb[LDV + rowB], vb[2 * LDV + rowB], vb[3 * LDV + rowB])};
+      float acc[1][2 * kSB];
+      dispatch_kk<KM>(kw, [&](auto K1, auto K2) {
+        f.template pass<decltype(K1)::value, decltype(K2)::value>(an_s + 16 * blk, ad_s + 16 * blk, vr, acc);
+      });
+      LR::template run<1>(acc, lane);
+      const int s = blk * kSB + osmp;
+      if (pvalid && writer && s < nvalid) {
+        const int idx = s * LDV + p;
+        float gval = fmaf(-2.0f, acc[0][0], DIR[idx]);
+        const long long bs = b0 + s;
+        bool done = false;
+        if (k == 0) {
+          const long long row = bs * T + t;
+          a.gsn[row * H + p] = GSN[idx];
+          a.gsd[row * H + p] = GSD[idx];
+          if (t == 0) {
+            a.gh0[bs * H + p] = gval;
+            done = true;
+          } else {
+            gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
+          }
+        }
+        if (!done) prep(rsm, vsm, vsn, an_m, ad_m, s, gval, k == 0);
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (--k < 0) {
+      k = U - 1;
+      --t;
+    }
+  }
+
+  // synapse partials at their dense positions (skipped synapses are never written)
+  float* part = a.part + (long long)grp * 4 * HP * HP;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = r ? rowB : rowA;
+#pragma unroll
+    for (int j = 0; j < KM; ++j) {
+      const int qi = tv.bidx[(tid * 2 + r) * KM + j];
+      if (qi < 0) continue;
+      const int idx = row * HP + qi;
+      const float v0 = f.Gwe[r][j].x + f.Gwe[r][j].y, v1 = f.Gwp[r][j].x + f.Gwp[r][j].y;
+      const float v2 = f.Gdz[r][j].x + f.Gdz[r][j].y, v3 = f.Gdzv[r][j].x + f.Gdzv[r][j].y;
+      if (a.accumulate) {
+        part[idx] += v0;
+        part[HP * HP + idx] += v1;
+        part[2 * HP * HP + idx] += v2;
+        part[3 * HP * HP + idx] += v3;
+      } else {
+        part[idx] = v0;
+        part[HP * HP + idx] = v1;
+        part[2 * HP * HP + idx] = v2;
+        part[3 * HP * HP + idx] = v3;
+      }
+    }
+  }
+  // per-neuron sums, fixed order over the lanes of the pair
+  for (int i = tid; i < 5 * HP * kTPC; i += NT) red[i] = 0.f;
+  __syncthreads();
+  if (writer) {
+    red[(0 * HP + p) * kTPC + g] = gcm;
+    red[(1 * HP + p) * kTPC + g] = ggl;
+    red[(2 * HP + p) * kTPC + g] = gvl;
+    red[(3 * HP + p) * kTPC + g] = san;
+    red[(4 * HP + p) * kTPC + g] = sad;
+  }
+  __syncthreads();
+  if (tid < HP) {
+    float* pn = a.partn + (long long)grp * 5 * HP;
+#pragma unroll
+    for (int kk = 0; kk < 5; ++kk) {
+      float sum = 0.f;
+      for (int l = 0; l < kTPC; ++l) sum += red[(kk * HP + tid) * kTPC + l];
+      pn[kk * HP + tid] = a.accumulate ? pn[kk * HP + tid] + sum : sum;
+    }
+  }
+}
+
+template <typename K, typename Args>
+cudaError_t launch_plain(K kernel, const Args& a, const SlotTablesView& tv, int grid, int threads, size_t smem,
+                         cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kernel<<<grid, threads, smem, st>>>(a, tv);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t sparse_tables_bytes(int HP) {
+  size_t at[9];
+  return tables_layout(HP, at);
+}
+
+int sparse_max_synapses_per_neuron(int HP) { return HP == 64 ? kTPC * slots_max<64>() : kTPC * slots_max<32>(); }
+
+void plan_sparse(RecPlan& p, int B, int num_sms) {
+  const int HP = p.HP;  // 32 or 64
+  const int LDV = HP + 4;
+  const int blocks = (B + kSB - 1) / kSB;
+  const size_t smem_cap = 227 * 1024 - 1024;
+  // backward: 4 neuron-major adjoint slabs + 8 [ns][LDV] slabs + the reduction area
+  auto bwd_bytes = [&](int ns) {
+    const int S = 4 * neuron_stride4(ns);
+    return ((size_t)4 * HP * S + 8 * (size_t)ns * LDV + 5 * HP * kTPC) * sizeof(float);
+  };
+  int cap = 1;
+  while (bwd_bytes((cap + 1) * kSB) <= smem_cap) ++cap;
+  // blocks per CTA: as many waves as the cap forces, spread evenly over them
+  const long long per_wave = (long long)num_sms * cap;
+  const long long waves = (blocks + per_wave - 1) / per_wave;
+  int per = (int)((blocks + waves * num_sms - 1) / (waves * num_sms));
+  if (per > cap) per = cap;
+  if (per < 1) per = 1;
+  const int ns = per * kSB;
+  const int S = 4 * neuron_stride4(ns);
+  p.sparse = true;
+  p.ns_fwd = p.ns_bwd = ns;
+  p.grid_fwd = p.grid_bwd = (B + ns - 1) / ns;
+  p.threads_fwd = p.threads_bwd = 4 * HP;
+  p.slots_bwd = p.grid_bwd;
+  p.smem_fwd = ((size_t)2 * HP * S + 2 * (size_t)ns * LDV) * sizeof(float);
+  p.smem_bwd = bwd_bytes(ns);
+  p.tanh_space = true;
+}
+
+cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st) {
+  const SlotTablesView tv = tables_view(tables, pa.HP);
+  if (pa.HP == 64)
+    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.sigma, pa.mu, pa.H);
+  else
+    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.sigma, pa.mu, pa.H);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sparse_fwd(const RecFwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st) {
+  const SlotTablesView tv = tables_view(const_cast<void*>(tables), p.HP);
+  return p.HP == 64 ? launch_plain(rec_fwd_sparse<64>, a, tv, p.grid_fwd, p.threads_fwd, p.smem_fwd, st)
+                    : launch_plain(rec_fwd_sparse<32>, a, tv, p.grid_fwd, p.threads_fwd, p.smem_fwd, st);
+}
+
+cudaError_t launch_sparse_bwd(const RecBwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st) {
+  const SlotTablesView tv = tables_view(const_cast<void*>(tables), p.HP);
+  return p.HP == 64 ? launch_plain(rec_bwd_sparse<64>, a, tv, p.grid_bwd, p.threads_bwd, p.smem_bwd, st)
+                    : launch_plain(rec_bwd_sparse<32>, a, tv, p.grid_bwd, p.threads_bwd, p.smem_bwd, st);
+}
+
+}  // namespace ltc

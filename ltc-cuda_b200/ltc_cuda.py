@@ -29,6 +29,7 @@ from __future__ import annotations
 import ctypes
 import logging
 import os
+import threading
 from typing import List, Optional, Sequence
 
 import torch
@@ -40,6 +41,7 @@ LIB_PATH = os.environ.get("LTC_SM100_LIB", os.path.join(_HERE, "libltc_sm100.so"
 
 LTC_FLAG_FORCE_WIDE = 1
 LTC_FLAG_LEAN_SAVE = 2
+LTC_FLAG_SKIP_ZERO_SYNAPSES = 4
 LTC_LEAN_CHUNK_SHIFT = 8
 
 
@@ -185,6 +187,52 @@ def set_lean_save(on: bool, chunk_steps: int = 0) -> None:
         _flags |= LTC_FLAG_LEAN_SAVE | ((int(chunk_steps) & 0xFFFF) << LTC_LEAN_CHUNK_SHIFT)
 
 
+_call_flags = threading.local()
+
+
+class skip_zero_synapses:
+    """Context manager: solver calls made inside it (forward, and the backward of those
+    forwards) skip recurrent synapses whose ``w_pos`` and ``w_erev`` are both zero
+    (``LTC_FLAG_SKIP_ZERO_SYNAPSES``).  The solver's gradients of ``w_pos``, ``w_erev``,
+    ``mu`` and ``sigma`` are then zero at those positions instead of the dense values --
+    use it only where those entries are discarded, as when ``w_pos = softplus(w) * mask``
+    (the module's transforms).  Other outputs are unchanged."""
+
+    def __init__(self, on: bool = True):
+        self.on = bool(on)
+
+    def __enter__(self):
+        self.prev = getattr(_call_flags, "extra", 0)
+        _call_flags.extra = (self.prev | LTC_FLAG_SKIP_ZERO_SYNAPSES) if self.on else \
+            (self.prev & ~LTC_FLAG_SKIP_ZERO_SYNAPSES)
+        return self
+
+    def __exit__(self, *exc):
+        _call_flags.extra = self.prev
+        return False
+
+
+# The synapse-skipping kernels hold at most this many nonzero synapses per neuron
+# (incoming and outgoing) for 32 < H <= 64; for H <= 32 any mask fits.  A call that
+# exceeds it gets NaN outputs from the kernels, so callers check first.
+SKIP_MAX_SYNAPSES_PER_NEURON = 48
+
+
+def skip_zero_synapses_fits(mask: torch.Tensor) -> bool:
+    """True when the (H, H) nonzero pattern ``mask`` fits the synapse-skipping kernels."""
+    H = mask.shape[0]
+    if H > 64:
+        return True  # the flag is ignored above H = 64 (dense kernels run)
+    if H <= 32:
+        return True
+    nz = mask != 0
+    return int(torch.maximum(nz.sum(0).max(), nz.sum(1).max()).item()) <= SKIP_MAX_SYNAPSES_PER_NEURON
+
+
+def _call_flags_now() -> int:
+    return _flags | getattr(_call_flags, "extra", 0)
+
+
 KERNEL_NAMES = ("pack_fwd", "sensory_fwd", "recurrent_fwd", "pack_bwd", "recurrent_bwd", "sensory_bwd",
                 "finish", "preamble_fwd", "preamble_bwd")
 
@@ -264,7 +312,7 @@ class _CudaModule:
         outputs = torch.empty(B, T, H, device=dev, dtype=torch.float32)
         if B == 0 or T == 0 or int(ode_unfolds) <= 0:
             return _degenerate_forward(x, h0, outputs, save_intermediates)
-        dims = make_dims(B, T, D, H, ode_unfolds, epsilon, _flags)
+        dims = make_dims(B, T, D, H, ode_unfolds, epsilon, _call_flags_now())
         with torch.cuda.device(dev):
             pl = plan(dims)
             h_final = torch.empty(B, H, device=dev, dtype=torch.float32)

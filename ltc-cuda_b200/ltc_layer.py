@@ -56,6 +56,9 @@ class TrueLiquidTimeConstant(nn.Module):
         self.sensory_sparsity = sensory_sparsity
         self.input_mapping = input_mapping
         self.epsilon = epsilon
+        # let the solver skip masked synapses (their solver-level gradients are discarded
+        # by the mask); a plain attribute, not part of the state dict
+        self.skip_zero_synapses = sparsity < 1.0
         H, D = hidden_dim, input_dim
 
         self.w = nn.Parameter(torch.empty(H, H).uniform_(0.001, 1.0))
@@ -121,10 +124,23 @@ class TrueLiquidTimeConstant(nn.Module):
         if _solver is ltc_cuda.ltc_cuda_forward and not (x.is_cuda and x.dtype == torch.float32):
             raise RuntimeError(f"TrueLiquidTimeConstant: the sm_100a solver needs fp32 CUDA input "
                                f"(got {x.dtype} on {x.device}); there is no CPU fallback")
-        outputs, state = _solver(x, state, w_pos, w_erev, self.mu, self.sigma, self.sensory_mu,
-                                 self.sensory_sigma, self.sensory_erev, sensory_w_pos, cm_t, gleak_pos,
-                                 self.vleak, self.ode_unfolds, self.epsilon)
+        # w_pos = softplus(w) * mask: the solver's gradients at masked synapses are
+        # multiplied by zero on the way to w and erev, so the solver may skip them
+        with ltc_cuda.skip_zero_synapses(self.skip_zero_synapses and self._skip_fits()):
+            outputs, state = _solver(x, state, w_pos, w_erev, self.mu, self.sigma, self.sensory_mu,
+                                     self.sensory_sigma, self.sensory_erev, sensory_w_pos, cm_t, gleak_pos,
+                                     self.vleak, self.ode_unfolds, self.epsilon)
         return outputs, (state, state)
+
+    def _skip_fits(self) -> bool:
+        """Whether the solver's synapse-skipping kernels can hold this mask (checked
+        once per mask version; one device sync the first time)."""
+        m = self.sparsity_mask
+        key = (m.data_ptr(), m._version, tuple(m.shape))
+        if getattr(self, "_skip_key", None) != key:
+            self._skip_ok = ltc_cuda.skip_zero_synapses_fits(m)
+            self._skip_key = key
+        return self._skip_ok
 
     def train(self, mode: bool = True):
         if mode:

@@ -1,0 +1,193 @@
+"""GPU parity of the zero-synapse-skipping path (LTC_FLAG_SKIP_ZERO_SYNAPSES, H <= 64).
+
+With the flag, the solver visits only synapses whose w_pos or w_erev is nonzero.
+Every output must match the reference restatement (the oracle, and the golden
+fixtures the reference produced) exactly as the dense path does, except the
+gradients of w_pos / w_erev at the skipped positions, which are zero by contract
+(mu / sigma gradients are zero there in the dense solve as well, since dL/dz = 0).
+Module-level gradients -- what training uses -- are unaffected: the module multiplies
+those entries by its mask.  Tolerances are the parity tests' (forward max-abs 1e-3,
+gradients rtol 5e-2 / atol 1e-2, normalised error < 2e-3).
+"""
+import pytest
+import torch
+
+import ltc_cuda
+import ltc_layer
+import synth
+from golden_io import Case, FN, case_names
+from ltc_testlib import FWD_ATOL, assert_grads_close, cuda_solver, oracle_solver, rel_err
+from oracle import ltc_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+SMALL_H = [n for n in case_names() if Case(n).meta["H"] <= 64]
+
+
+def _sparse_solver(inp, U, eps, gout=None, gh=None, backward=True):
+    with ltc_cuda.skip_zero_synapses():
+        return cuda_solver(inp, U, eps, gout=gout, gh=gh, backward=backward)
+
+
+def _expect_masked(ref, inp):
+    """Oracle gradients with the skipped positions' w_pos / w_erev entries zeroed."""
+    zero = (inp["w_pos"] == 0) & (inp["w_erev"] == 0)
+    out = dict(ref)
+    for k in ("w_pos", "w_erev"):
+        out[k] = torch.where(zero.to(ref[k].device), torch.zeros_like(ref[k]), ref[k])
+    for k in ("mu", "sigma"):  # exactly zero in the dense solve too
+        assert float(ref[k].to(zero.device)[zero].abs().max().item() if zero.any() else 0.0) < 1e-12, k
+    return out
+
+
+def _check(inp, U, gout, gh, ctx, device="cpu", chunk=None):
+    out, h, g = _sparse_solver(inp, U, 1e-8, gout=gout, gh=gh)
+    ro, rh, rg = oracle_solver(inp, U, 1e-8, gout=gout, gh=gh, device=device, chunk=chunk)
+    assert (out.cpu() - ro.cpu()).abs().max().item() < FWD_ATOL, ctx
+    assert (h.cpu() - rh.cpu()).abs().max().item() < FWD_ATOL, ctx
+    rg = _expect_masked({k: v.cpu() for k, v in rg.items()}, {k: v.cpu() for k, v in inp.items()})
+    assert_grads_close(g, rg, ctx=ctx)
+    for k in FN:
+        assert rel_err(g[k], rg[k]) < 2e-3, f"{ctx} {k}: {rel_err(g[k], rg[k]):.2e}"
+    return out, h, g
+
+
+def test_plan_uses_sparse_kernels():
+    dims = ltc_cuda.make_dims(64, 4, 16, 64, 6, 1e-8, ltc_cuda.LTC_FLAG_SKIP_ZERO_SYNAPSES)
+    assert ltc_cuda.plan(dims).bwd_workspace_bytes > ltc_cuda.plan(ltc_cuda.make_dims(64, 4, 16, 64, 6, 1e-8)).bwd_workspace_bytes
+
+
+@pytest.mark.parametrize("name", SMALL_H)
+def test_golden_solver_level_sparse(name):
+    c = Case(name)
+    if "gout" not in c.a:
+        out, h, _ = _sparse_solver(c.solver_inputs, c.meta["U"], c.meta["epsilon"], backward=False)
+        assert (out.cpu() - c.a["out"]).abs().max().item() < FWD_ATOL
+        return
+    out, h, g = _sparse_solver(c.solver_inputs, c.meta["U"], c.meta["epsilon"], gout=c.get("gout"), gh=c.get("gh"))
+    assert (out.cpu() - c.a["out"]).abs().max().item() < FWD_ATOL
+    assert (h.cpu() - c.a["h"]).abs().max().item() < FWD_ATOL
+    ref = _expect_masked(c.solver_grads, c.solver_inputs)
+    assert_grads_close(g, ref, ctx=name)
+    for k in FN:
+        assert rel_err(g[k], ref[k]) < 1e-3, f"{name} {k}: {rel_err(g[k], ref[k]):.2e}"
+
+
+def _inputs(D, H, B, T, U, density, seed, mask=None):
+    p = synth.make_params(D, H, density, 0.5, seed=seed)
+    if mask is not None:
+        p["sparsity_mask"] = mask
+        p["erev"] = p["erev"].abs().clamp_min(1.0) * torch.where(torch.rand(H, H) < 0.5, 1.0, -1.0) * mask
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, T, D, generator=g)
+    inp = {k: v.detach() for k, v in orc.module_preamble(p, x, 1 / 30, U).items()}
+    inp["state"] = torch.randn(B, H, generator=g) * 0.3
+    return inp, torch.randn(B, T, H, generator=g), torch.randn(B, H, generator=g)
+
+
+@pytest.mark.parametrize("H,density", [(64, 0.5), (64, 0.2), (48, 0.5), (33, 0.5), (32, 0.5), (32, 1.0),
+                                       (17, 0.3), (8, 0.5), (1, 1.0)])
+def test_densities_vs_oracle(H, density):
+    inp, gout, gh = _inputs(12, H, 9, 5, 4, density, seed=H * 7 + int(density * 10))
+    _check(inp, 4, gout, gh, f"H{H} d{density}")
+
+
+def test_capacity_boundary_48_per_neuron():
+    """Every row and column at exactly the capacity (48 of 64): a circulant band."""
+    H = 64
+    idx = torch.arange(H)
+    mask = (((idx[None, :] - idx[:, None]) % H) < ltc_cuda.SKIP_MAX_SYNAPSES_PER_NEURON).float()
+    assert ltc_cuda.skip_zero_synapses_fits(mask)
+    inp, gout, gh = _inputs(10, H, 7, 4, 3, 0.5, seed=17, mask=mask)
+    _check(inp, 3, gout, gh, "capacity")
+
+
+def test_over_capacity_gives_nan_and_module_falls_back():
+    """A mask beyond the capacity poisons the outputs with NaN (a loud failure, not a
+    wrong number); the module checks the mask and runs the dense kernels instead."""
+    H = 64
+    mask = (torch.rand(H, H, generator=torch.Generator().manual_seed(9)) < 0.5).float()
+    mask[3, :50] = 1.0
+    assert not ltc_cuda.skip_zero_synapses_fits(mask)
+    inp, gout, gh = _inputs(10, H, 5, 3, 3, 0.5, seed=19, mask=mask)
+    out, h, g = _sparse_solver(inp, 3, 1e-8, gout=gout, gh=gh)
+    assert torch.isnan(out).all() and torch.isnan(h).all()
+    assert all(torch.isnan(g[k]).any() for k in ("x_seq", "w_pos", "mu", "cm_t"))
+    torch.manual_seed(8)
+    m = ltc_layer.TrueLiquidTimeConstant(16, H, sparsity=0.9).cuda()
+    assert not ltc_cuda.skip_zero_synapses_fits(m.sparsity_mask)
+    out, (hh, _) = m(torch.randn(3, 4, 16, device="cuda"))
+    out.sum().backward()
+    assert torch.isfinite(out).all() and all(torch.isfinite(q.grad).all() for q in m.parameters())
+
+
+def test_empty_rows_and_columns():
+    """Neurons with no outgoing (rows) or incoming (columns) synapses, and an all-zero block."""
+    H = 64
+    mask = (torch.rand(H, H, generator=torch.Generator().manual_seed(3)) < 0.5).float()
+    mask[5] = 0.0
+    mask[:, 9] = 0.0
+    mask[40:, :] = 0.0
+    inp, gout, gh = _inputs(8, H, 6, 4, 3, 0.5, seed=11, mask=mask)
+    _check(inp, 3, gout, gh, "empty rows/cols")
+    inp0, gout0, gh0 = _inputs(8, H, 6, 4, 3, 0.5, seed=12, mask=torch.zeros(H, H))
+    _check(inp0, 3, gout0, gh0, "all-zero mask")
+
+
+@pytest.mark.parametrize("cfg,B,T", [("c1", 16, None), ("c3", 64, 32)])
+def test_configs_vs_oracle(cfg, B, T):
+    c = synth.CONFIGS[cfg]
+    p, x = synth.make_workload(c, batch=B)
+    if T is not None:
+        x = x[:, :T].contiguous()
+    inp = {k: v.detach() for k, v in orc.module_preamble(p, x, c.dt, c.U).items()}
+    inp["state"] = torch.zeros(x.shape[0], c.H)
+    g = torch.Generator().manual_seed(7)
+    _check(inp, c.U, torch.randn(x.shape[0], x.shape[1], c.H, generator=g), None, cfg)
+
+
+def test_multi_wave_and_odd_batch():
+    inp, gout, gh = _inputs(8, 64, 6001, 2, 3, 0.5, seed=5)
+    _check(inp, 3, gout, gh, "B6001", device="cuda", chunk=1500)
+
+
+def test_determinism_and_batch_split():
+    inp, gout, gh = _inputs(16, 64, 300, 6, 6, 0.5, seed=21)
+    runs = [_sparse_solver(inp, 6, 1e-8, gout=gout, gh=gh) for _ in range(2)]
+    assert torch.equal(runs[0][0], runs[1][0])
+    for k in FN:
+        assert torch.equal(runs[0][2][k], runs[1][2][k]), k
+    part = {k: (v[100:200] if k in ("x_seq", "state") else v) for k, v in inp.items()}
+    o, h, _ = _sparse_solver(part, 6, 1e-8, backward=False)
+    assert torch.equal(o, runs[0][0][100:200])
+
+
+def test_lean_save_with_sparse():
+    inp, gout, gh = _inputs(16, 64, 40, 9, 3, 0.5, seed=31)
+    ref = _sparse_solver(inp, 3, 1e-8, gout=gout, gh=gh)
+    ltc_cuda.set_lean_save(True, chunk_steps=4)
+    try:
+        got = _sparse_solver(inp, 3, 1e-8, gout=gout, gh=gh)
+    finally:
+        ltc_cuda.set_lean_save(False)
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
+    for k in FN:
+        assert rel_err(got[2][k], ref[2][k]) < 1e-5, k
+
+
+def test_module_grads_match_dense_path():
+    """Module level: the skipping path gives the same parameter gradients as the dense one."""
+    torch.manual_seed(4)
+    m = ltc_layer.TrueLiquidTimeConstant(40, 64, sparsity=0.4).cuda()
+    assert m.skip_zero_synapses
+    x = torch.randn(7, 10, 40, device="cuda")
+    grads = []
+    for skip in (True, False):
+        m.skip_zero_synapses = skip
+        m.zero_grad()
+        out, (h, _) = m(x)
+        (out.sum() + h.square().sum()).backward()
+        grads.append({n: q.grad.clone() for n, q in m.named_parameters()})
+    for n in grads[0]:
+        a, b = grads[0][n], grads[1][n]
+        assert torch.allclose(a, b, rtol=1e-4, atol=1e-5), f"{n}: {(a - b).abs().max().item():.3e}"
