@@ -7,23 +7,24 @@
 // declares those gradients unused; these kernels then visit only the nonzero
 // synapses and the finish kernel writes zeros at the skipped positions.
 //
-// Layout.  8 lanes share a PAIR of neurons (rows in the backward, columns in the
-// forward): the c-th heaviest and the c-th lightest by nonzero count, so every
-// pair carries a similar total.  Each lane holds up to KM synapses of each
-// neuron, taken from the neuron's nonzero list (entry e -> lane e % 8, slot
-// e / 8); a warp (4 pairs) runs its slot counts (K1, K2) -- the largest of its
-// heavy / light neurons' ceil(count / 8) -- as compile-time constants, chosen by
-// a switch at the top of each sample block, so no per-slot branch is issued.
+// Layout.  TPC lanes (8 in the backward, 16 in the forward) share a PAIR of
+// neurons (rows in the backward, columns in the forward): the c-th heaviest and
+// the c-th lightest by nonzero count, so every pair carries a similar total.
+// Each lane holds up to KM synapses of each neuron, taken from the neuron's
+// nonzero list (entry e -> lane e % TPC, slot e / TPC); a warp runs its slot
+// counts (K1, K2) -- the largest of its heavy / light neurons' ceil(count / TPC)
+// -- as compile-time constants, chosen by a jump table at the top of each sample
+// block, so no per-slot branch is issued.
 // The per-neuron vectors the synapse pass gathers from (v in the forward, the
 // adjoints in the backward) are stored neuron-major, four samples per float4,
 // with an odd number of float4 per neuron; lists are ordered round-robin over the
-// residue mod 8, so the eight lanes of a quarter-warp (one pair) gather from
-// distinct bank groups.  The packed f32x2 pairs run over two SAMPLES of one
+// residue mod 8, so the eight lanes of a quarter-warp (consecutive entries of one
+// neuron's list) gather from distinct bank groups.  The packed f32x2 pairs run over two SAMPLES of one
 // synapse (adjacent in the gathered float4), with the synapse constants
 // duplicated in both halves, so forming the pairs costs no register moves.
 //
-// Capacity: KM slots per neuron and lane (HP = 64: 6, i.e. at most 48 nonzero
-// synapses per neuron; HP = 32: 4, any mask).  The table builder checks it; a
+// Capacity: at most 48 nonzero synapses per neuron at HP = 64 (TPC * KM); any
+// mask at HP = 32.  The table builder checks it; a
 // call whose mask exceeds it writes NaN to every output of the kernels (state,
 // outputs, gradients) instead of a wrong number -- callers check the mask first
 // (ltc_cuda.skip_zero_synapses does).
@@ -40,31 +41,37 @@ namespace ltc {
 namespace {
 
 constexpr int kSB = 4;   // samples per block (one float4 of a neuron-major vector)
-constexpr int kTPC = 8;  // lanes per neuron pair
-template <int HP>
-constexpr int slots_max() { return HP == 64 ? 6 : 4; }
+// lanes per neuron pair and slots per neuron and lane: the forward (side 1) uses
+// 16 lanes per pair (512 threads at HP = 64; its registers allow it, and the
+// MUFU-bound pass wants the warps), the backward (side 0) 8 lanes per pair
+// (256 threads; 16 registers per slot).  Capacity is 48 synapses per neuron at
+// HP = 64 and 32 (every mask) at HP = 32 either way.
+constexpr int kCap64 = 48;
+__host__ __device__ constexpr int side_tpc(int side) { return side ? 16 : 8; }
+__host__ __device__ constexpr int side_km(int HP, int side) { return (HP == 64 ? kCap64 : 32) / side_tpc(side); }
+__host__ __device__ constexpr int side_nt(int HP, int side) { return HP / 2 * side_tpc(side); }
 
 // slot tables inside the caller's workspace (see sparse_tables_bytes)
 struct SlotTablesView {
   int* fneu;      // [HP]          neuron of (pair c, r) at 2c + r (forward: column q)
   int* fk;        // [warps]       K1 | K2 << 8
-  float4* fpack;  // [NT][2][KM]   (sigma/2, -sigma*mu/2, w_pos/2, w_erev/2)
-  int* fidx;      // [NT][2][KM]   presynaptic neuron p, -1 = padding
+  float4* fpack;  // [NTf][2][KMf] (sigma/2, -sigma*mu/2, w_pos/2, w_erev/2)
+  int* fidx;      // [NTf][2][KMf] presynaptic neuron p, -1 = padding
   int* bneu;      // [HP]          backward: row p
   int* bk;        // [warps]
-  float4* bpack;  // [NT][2][KM]   (-sigma/2, sigma*mu/2, w_pos, w_erev)
-  int* bidx;      // [NT][2][KM]   postsynaptic neuron q, -1 = padding
-  int* overflow;  // [1]           1 if a neuron has more than 8 * KM nonzero synapses
+  float4* bpack;  // [NTb][2][KMb] (-sigma/2, sigma*mu/2, w_pos, w_erev)
+  int* bidx;      // [NTb][2][KMb] postsynaptic neuron q, -1 = padding
+  int* overflow;  // [1]           1 if a neuron has more nonzero synapses than the capacity
 };
 
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
 // byte offsets of the table arrays; returns the total size
 inline size_t tables_layout(int HP, size_t (&at)[9]) {
-  const int NT = 4 * HP, KM = HP == 64 ? 6 : 4, NW = NT / 32;
-  const size_t sz[9] = {HP * sizeof(int), NW * sizeof(int), (size_t)NT * 2 * KM * sizeof(float4),
-                        (size_t)NT * 2 * KM * sizeof(int), HP * sizeof(int), NW * sizeof(int),
-                        (size_t)NT * 2 * KM * sizeof(float4), (size_t)NT * 2 * KM * sizeof(int), sizeof(int)};
+  const size_t nf = (size_t)side_nt(HP, 1) * 2 * side_km(HP, 1), nb = (size_t)side_nt(HP, 0) * 2 * side_km(HP, 0);
+  const size_t sz[9] = {HP * sizeof(int), side_nt(HP, 1) / 32 * sizeof(int), nf * sizeof(float4), nf * sizeof(int),
+                        HP * sizeof(int), side_nt(HP, 0) / 32 * sizeof(int), nb * sizeof(float4), nb * sizeof(int),
+                        sizeof(int)};
   size_t o = 0;
   for (int i = 0; i < 9; ++i) {
     at[i] = o;
@@ -98,7 +105,7 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
                                                           const float* __restrict__ w_erev,
                                                           const float* __restrict__ sigma,
                                                           const float* __restrict__ mu, int H) {
-  constexpr int KM = slots_max<HP>(), NPAIR = HP / 2, PPW = 32 / kTPC;  // pairs per warp
+  constexpr int NPAIR = HP / 2, CAP = HP == 64 ? kCap64 : 32;
   __shared__ uint64_t nz[2][HP];  // [0] bit q of row p; [1] bit p of column q
   __shared__ int cnt[2][HP];
   __shared__ int order[2][HP];    // neurons by count, descending
@@ -131,7 +138,7 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
   __syncthreads();
   if (tid == 0) {
     int over = 0;
-    for (int i = 0; i < 2 * HP; ++i) over |= cnt[i / HP][i % HP] > kTPC * KM;
+    for (int i = 0; i < 2 * HP; ++i) over |= cnt[i / HP][i % HP] > CAP;
     *tv.overflow = over;
   }
   // neuron of (pair c, r): r = 0 the c-th heaviest, r = 1 the c-th lightest
@@ -139,14 +146,16 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
     const int s = i / HP, k = i % HP, c = k / 2, r = k % 2;
     (s ? tv.fneu : tv.bneu)[k] = order[s][r ? HP - 1 - c : c];
   }
-  for (int i = tid; i < 2 * (NPAIR / PPW); i += blockDim.x) {  // slot counts per warp
-    const int s = i / (NPAIR / PPW), w = i % (NPAIR / PPW);
-    int k1 = 0, k2 = 0;
-    for (int c = PPW * w; c < PPW * w + PPW; ++c) {
-      k1 = max(k1, min(KM, (cnt[s][order[s][c]] + kTPC - 1) / kTPC));
-      k2 = max(k2, min(KM, (cnt[s][order[s][HP - 1 - c]] + kTPC - 1) / kTPC));
+  for (int s = 0; s < 2; ++s) {  // slot counts per warp
+    const int TPC = side_tpc(s), KM = side_km(HP, s), PPW = 32 / TPC;
+    for (int w = tid; w < NPAIR / PPW; w += blockDim.x) {
+      int k1 = 0, k2 = 0;
+      for (int c = PPW * w; c < PPW * w + PPW; ++c) {
+        k1 = max(k1, min(KM, (cnt[s][order[s][c]] + TPC - 1) / TPC));
+        k2 = max(k2, min(KM, (cnt[s][order[s][HP - 1 - c]] + TPC - 1) / TPC));
+      }
+      (s ? tv.fk : tv.bk)[w] = k1 | (k2 << 8);
     }
-    (s ? tv.fk : tv.bk)[w] = k1 | (k2 << 8);
   }
   // lists: one thread per (side, pair, r); entries round-robin over residues mod 8
   for (int i = tid; i < 2 * HP; i += blockDim.x) {
@@ -155,11 +164,12 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
     const uint64_t m = nz[s][n];
     float4* pk = s ? tv.fpack : tv.bpack;
     int* ix = s ? tv.fidx : tv.bidx;
+    const int TPC = side_tpc(s), KM = side_km(HP, s);
     int next[8];
 #pragma unroll
     for (int b = 0; b < 8; ++b) next[b] = b;
     int e = 0;
-    const int total = min(__popcll(m), kTPC * KM);
+    const int total = min(__popcll(m), TPC * KM);
     while (e < total) {
       for (int b = 0; b < 8 && e < total; ++b) {
         int o = next[b];
@@ -169,15 +179,15 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
         const int p = s ? o : n, q = s ? n : o;  // synapse (p, q)
         const long long j = (long long)p * H + q;
         const float sg = sigma[j], wp = w_pos[j], we = w_erev[j];
-        const int slot = ((c * kTPC + e % kTPC) * 2 + r) * KM + e / kTPC;
+        const int slot = ((c * TPC + e % TPC) * 2 + r) * KM + e / TPC;
         pk[slot] = s ? make_float4(0.5f * sg, -0.5f * sg * mu[j], 0.5f * wp, 0.5f * we)
                      : make_float4(-0.5f * sg, 0.5f * sg * mu[j], wp, we);
         ix[slot] = o;
         ++e;
       }
     }
-    for (; e < kTPC * KM; ++e) {
-      const int slot = ((c * kTPC + e % kTPC) * 2 + r) * KM + e / kTPC;
+    for (; e < TPC * KM; ++e) {
+      const int slot = ((c * TPC + e % TPC) * 2 + r) * KM + e / TPC;
       pk[slot] = make_float4(0.f, 0.f, 0.f, 0.f);
       ix[slot] = -1;
     }
@@ -191,47 +201,43 @@ __host__ __device__ inline int neuron_stride4(int ns) {
 }
 
 // the warp's (K1, K2) -> the compile-time pass (K1 >= K2, both <= KM): one jump
-// table (kw = K1 | K2 << 8), not a chain of compares
+// table on kw = K1 | K2 << 8, not a chain of compares
+template <int V>
+using IC = std::integral_constant<int, V>;
 template <int KM, typename Fn>
 __device__ __forceinline__ void dispatch_kk(int kw, Fn&& fn) {
-  using I0 = std::integral_constant<int, 0>;
   switch (kw) {
-    case 0: fn(I0{}, I0{}); return;
-    case 1: fn(std::integral_constant<int, 1>{}, I0{}); return;
-    case 1 | (1 << 8): fn(std::integral_constant<int, 1>{}, std::integral_constant<int, 1>{}); return;
-    case 2: fn(std::integral_constant<int, 2>{}, I0{}); return;
-    case 2 | (1 << 8): fn(std::integral_constant<int, 2>{}, std::integral_constant<int, 1>{}); return;
-    case 2 | (2 << 8): fn(std::integral_constant<int, 2>{}, std::integral_constant<int, 2>{}); return;
-    case 3: fn(std::integral_constant<int, 3>{}, I0{}); return;
-    case 3 | (1 << 8): fn(std::integral_constant<int, 3>{}, std::integral_constant<int, 1>{}); return;
-    case 3 | (2 << 8): fn(std::integral_constant<int, 3>{}, std::integral_constant<int, 2>{}); return;
-    case 3 | (3 << 8): fn(std::integral_constant<int, 3>{}, std::integral_constant<int, 3>{}); return;
-    case 4: fn(std::integral_constant<int, 4>{}, I0{}); return;
-    case 4 | (1 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 1>{}); return;
-    case 4 | (2 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 2>{}); return;
-    case 4 | (3 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 3>{}); return;
+    case 0 | (0 << 8): if constexpr (KM >= 0) { fn(IC<0>{}, IC<0>{}); return; } break;
+    case 1 | (0 << 8): if constexpr (KM >= 1) { fn(IC<1>{}, IC<0>{}); return; } break;
+    case 1 | (1 << 8): if constexpr (KM >= 1) { fn(IC<1>{}, IC<1>{}); return; } break;
+    case 2 | (0 << 8): if constexpr (KM >= 2) { fn(IC<2>{}, IC<0>{}); return; } break;
+    case 2 | (1 << 8): if constexpr (KM >= 2) { fn(IC<2>{}, IC<1>{}); return; } break;
+    case 2 | (2 << 8): if constexpr (KM >= 2) { fn(IC<2>{}, IC<2>{}); return; } break;
+    case 3 | (0 << 8): if constexpr (KM >= 3) { fn(IC<3>{}, IC<0>{}); return; } break;
+    case 3 | (1 << 8): if constexpr (KM >= 3) { fn(IC<3>{}, IC<1>{}); return; } break;
+    case 3 | (2 << 8): if constexpr (KM >= 3) { fn(IC<3>{}, IC<2>{}); return; } break;
+    case 3 | (3 << 8): if constexpr (KM >= 3) { fn(IC<3>{}, IC<3>{}); return; } break;
+    case 4 | (0 << 8): if constexpr (KM >= 4) { fn(IC<4>{}, IC<0>{}); return; } break;
+    case 4 | (1 << 8): if constexpr (KM >= 4) { fn(IC<4>{}, IC<1>{}); return; } break;
+    case 4 | (2 << 8): if constexpr (KM >= 4) { fn(IC<4>{}, IC<2>{}); return; } break;
+    case 4 | (3 << 8): if constexpr (KM >= 4) { fn(IC<4>{}, IC<3>{}); return; } break;
+    case 4 | (4 << 8): if constexpr (KM >= 4) { fn(IC<4>{}, IC<4>{}); return; } break;
+    case 5 | (0 << 8): if constexpr (KM >= 5) { fn(IC<5>{}, IC<0>{}); return; } break;
+    case 5 | (1 << 8): if constexpr (KM >= 5) { fn(IC<5>{}, IC<1>{}); return; } break;
+    case 5 | (2 << 8): if constexpr (KM >= 5) { fn(IC<5>{}, IC<2>{}); return; } break;
+    case 5 | (3 << 8): if constexpr (KM >= 5) { fn(IC<5>{}, IC<3>{}); return; } break;
+    case 5 | (4 << 8): if constexpr (KM >= 5) { fn(IC<5>{}, IC<4>{}); return; } break;
+    case 5 | (5 << 8): if constexpr (KM >= 5) { fn(IC<5>{}, IC<5>{}); return; } break;
+    case 6 | (0 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<0>{}); return; } break;
+    case 6 | (1 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<1>{}); return; } break;
+    case 6 | (2 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<2>{}); return; } break;
+    case 6 | (3 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<3>{}); return; } break;
+    case 6 | (4 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<4>{}); return; } break;
+    case 6 | (5 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<5>{}); return; } break;
+    case 6 | (6 << 8): if constexpr (KM >= 6) { fn(IC<6>{}, IC<6>{}); return; } break;
     default: break;
   }
-  if constexpr (KM >= 6) {
-    switch (kw) {
-      case 4 | (4 << 8): fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 4>{}); return;
-      case 5: fn(std::integral_constant<int, 5>{}, I0{}); return;
-      case 5 | (1 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 1>{}); return;
-      case 5 | (2 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 2>{}); return;
-      case 5 | (3 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 3>{}); return;
-      case 5 | (4 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 4>{}); return;
-      case 5 | (5 << 8): fn(std::integral_constant<int, 5>{}, std::integral_constant<int, 5>{}); return;
-      case 6: fn(std::integral_constant<int, 6>{}, I0{}); return;
-      case 6 | (1 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 1>{}); return;
-      case 6 | (2 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 2>{}); return;
-      case 6 | (3 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 3>{}); return;
-      case 6 | (4 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 4>{}); return;
-      case 6 | (5 << 8): fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 5>{}); return;
-      default: fn(std::integral_constant<int, 6>{}, std::integral_constant<int, 6>{}); return;
-    }
-  } else {
-    fn(std::integral_constant<int, 4>{}, std::integral_constant<int, 4>{});
-  }
+  fn(IC<KM>{}, IC<KM>{});
 }
 
 // 16-bit byte offsets of a lane's slots (two per register)
@@ -248,7 +254,7 @@ struct Offsets {
 // vbuf[2][HP][S] neuron-major states (S = 4 * neuron_stride4(ns)); snb/sdb [ns][LDV].
 template <int HP>
 struct SparseFwd {
-  static constexpr int KM = slots_max<HP>(), NT = 4 * HP, LDV = HP + 4;
+  static constexpr int TPC = side_tpc(1), KM = side_km(HP, 1), NT = side_nt(HP, 1), LDV = HP + 4;
   float2 sl2[2][KM], nm2[2][KM], wp2[2][KM], we2[2][KM];  // duplicated constants
   Offsets<2 * KM> off;
   float cwe[2], cwp[2];
@@ -290,10 +296,10 @@ struct SparseFwd {
 };
 
 template <int HP>
-__global__ void __launch_bounds__(4 * HP, 1) rec_fwd_sparse(RecFwdArgs a, SlotTablesView tv) {
+__global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a, SlotTablesView tv) {
   using F = SparseFwd<HP>;
-  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV;
-  using LR = LaneReduce<kTPC, 2 * kSB>;
+  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV, TPC = F::TPC;
+  using LR = LaneReduce<TPC, 2 * kSB>;
   extern __shared__ __align__(16) float smem[];
   const int ns = a.ns;
   const int S = 4 * neuron_stride4(ns);
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(4 * HP, 1) rec_fwd_sparse(RecFwdArgs a, SlotTa
   float* snb = vbuf + 2 * HP * S;     // [ns][LDV]
   float* sdb = snb + ns * LDV;        // [ns][LDV]
 
-  const int tid = threadIdx.x, lane = tid & 31, c = tid / kTPC;
+  const int tid = threadIdx.x, lane = tid & 31, c = tid / TPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
   const int b0 = blockIdx.x * ns;
   const int nvalid = min(ns, B - b0);
@@ -399,7 +405,7 @@ __global__ void __launch_bounds__(4 * HP, 1) rec_fwd_sparse(RecFwdArgs a, SlotTa
 // processed and the next one; VS[3], RS[2], DIR, GSN, GSD [ns][LDV] as in the dense kernel.
 template <int HP>
 struct SparseBwd {
-  static constexpr int KM = slots_max<HP>(), NT = 4 * HP, LDV = HP + 4;
+  static constexpr int TPC = side_tpc(0), KM = side_km(HP, 0), NT = side_nt(HP, 0), LDV = HP + 4;
   float2 sl2[2][KM], nm2[2][KM], wp2[2][KM], we2[2][KM];   // duplicated constants
   float2 Gwe[2][KM], Gwp[2][KM], Gdz[2][KM], Gdzv[2][KM];  // (even, odd) sample sums
   Offsets<2 * KM> off;
@@ -448,9 +454,9 @@ struct SparseBwd {
 };
 
 template <int HP>
-__global__ void __launch_bounds__(4 * HP, 1) rec_bwd_sparse(RecBwdArgs a, SlotTablesView tv) {
+__global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a, SlotTablesView tv) {
   using F = SparseBwd<HP>;
-  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV;
+  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV, kTPC = F::TPC;
   using LR = LaneReduce<kTPC, 2 * kSB>;
   extern __shared__ __align__(16) float smem[];
   const int ns = a.ns;
@@ -678,7 +684,6 @@ size_t sparse_tables_bytes(int HP) {
   return tables_layout(HP, at);
 }
 
-int sparse_max_synapses_per_neuron(int HP) { return HP == 64 ? kTPC * slots_max<64>() : kTPC * slots_max<32>(); }
 
 void plan_sparse(RecPlan& p, int B, int num_sms) {
   const int HP = p.HP;  // 32 or 64
@@ -688,7 +693,7 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
   // backward: 4 neuron-major adjoint slabs + 8 [ns][LDV] slabs + the reduction area
   auto bwd_bytes = [&](int ns) {
     const int S = 4 * neuron_stride4(ns);
-    return ((size_t)4 * HP * S + 8 * (size_t)ns * LDV + 5 * HP * kTPC) * sizeof(float);
+    return ((size_t)4 * HP * S + 8 * (size_t)ns * LDV + 5 * HP * side_tpc(0)) * sizeof(float);
   };
   int cap = 1;
   while (bwd_bytes((cap + 1) * kSB) <= smem_cap) ++cap;
@@ -703,7 +708,8 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
   p.sparse = true;
   p.ns_fwd = p.ns_bwd = ns;
   p.grid_fwd = p.grid_bwd = (B + ns - 1) / ns;
-  p.threads_fwd = p.threads_bwd = 4 * HP;
+  p.threads_fwd = side_nt(HP, 1);
+  p.threads_bwd = side_nt(HP, 0);
   p.slots_bwd = p.grid_bwd;
   p.smem_fwd = ((size_t)2 * HP * S + 2 * (size_t)ns * LDV) * sizeof(float);
   p.smem_bwd = bwd_bytes(ns);
