@@ -591,14 +591,30 @@ cudaError_t launch_grouped(void (*kernel)(Args), const Args& a, int grid, int th
   }
 }
 
+// Host-side bounds checks of a launch's sample grouping against the shared-memory
+// layout the kernels index (slabs of ns * LDV floats; sample s < ns; blocks of kSB;
+// at most kMaxBlk blocks per group with the cluster exchange): a plan that breaks
+// them is refused before any launch.
+template <int HP>
+bool grouping_ok(int B, int ns, int grid, size_t smem, size_t need_floats) {
+  const int CL = cluster_of<HP>();
+  return ns > 0 && ns % kSB == 0 && (long long)(grid / CL) * ns >= B && grid % CL == 0 &&
+         (CL == 1 || ns / kSB <= kMaxBlk) && smem >= need_floats * sizeof(float) && smem <= 227 * 1024;
+}
+
 template <int HP>
 cudaError_t launch_fast_fwd(const RecFwdArgs& a, const RecPlan& pl, cudaStream_t st) {
+  if (!grouping_ok<HP>(a.B, a.ns, pl.grid_fwd, pl.smem_fwd, (size_t)4 * a.ns * (HP + 4)))
+    return cudaErrorInvalidValue;
   return launch_grouped<cluster_of<HP>()>(rec_fwd_fast<HP>, a, pl.grid_fwd,
                                           Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>::NT, pl.smem_fwd, st);
 }
 
 template <int HP>
 cudaError_t launch_fast_bwd(const RecBwdArgs& a, const RecPlan& pl, cudaStream_t st) {
+  if (!grouping_ok<HP>(a.B, a.ns, pl.grid_bwd, pl.smem_bwd,
+                       (size_t)13 * a.ns * (HP + 4) + 5 * HP * (HP / 8)))
+    return cudaErrorInvalidValue;
   return launch_grouped<cluster_of<HP>()>(rec_bwd_fast<HP>, a, pl.grid_bwd,
                                           Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>::NT, pl.smem_bwd, st);
 }
