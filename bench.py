@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--seq", type=int, default=None, help="override the sequence length T (profiling captures)")
     ap.add_argument("--lean", type=int, default=0,
                     help="1: memory-lean training (step-boundary states saved, unfolds recomputed in the backward)")
+    ap.add_argument("--skip-zero", type=int, default=1,
+                    help="1 (default): the module lets the solver skip masked recurrent synapses (H <= 64); 0: dense")
     ap.add_argument("--graph", type=int, default=None,
                     help="1 (default): replay the whole step as a captured CUDA graph; 0: eager launches")
     return ap.parse_args()
@@ -300,7 +302,7 @@ def module_parity(run_ours, make_ours, ltc, p, cfg, dev):
 
 def rec_synapses(model, cfg) -> int:
     """Recurrent synapses per unfold the kernels visit (see ltc_cuda.skip_zero_synapses)."""
-    if getattr(model, "skip_zero_synapses", False) and cfg.H <= 64:
+    if getattr(model, "skip_zero_synapses", False) and cfg.H <= 64 and model._skip_fits():
         return int(model.sparsity_mask.count_nonzero().item())
     return cfg.H * cfg.H
 
@@ -405,6 +407,7 @@ def main():
     model = ltc_layer.TrueLiquidTimeConstant(cfg.D, cfg.H, dt=cfg.dt, ode_unfolds=cfg.U,
                                              sparsity=cfg.density, sensory_sparsity=cfg.sensory_density)
     model.load_state_dict(p)
+    model.skip_zero_synapses = model.skip_zero_synapses and bool(args.skip_zero)
     model = model.to(dev)
     bucket = FlatGradBucket(model.parameters())
     use_graph = bool(args.graph) if args.graph is not None else True

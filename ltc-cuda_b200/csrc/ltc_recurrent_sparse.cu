@@ -29,7 +29,8 @@
 // outputs, gradients) instead of a wrong number -- callers check the mask first
 // (ltc_cuda.skip_zero_synapses does).
 //
-// Tables are rebuilt on the device at every call (build_slots_kernel, one CTA),
+// Tables are rebuilt on the device at every call (build_slots_kernel, one CTA, a few
+// microseconds),
 // so the host never reads the mask and CUDA-graph capture stays possible.
 #include <cstdint>
 #include <type_traits>
@@ -51,15 +52,16 @@ __host__ __device__ constexpr int side_tpc(int side) { return side ? 16 : 8; }
 __host__ __device__ constexpr int side_km(int HP, int side) { return (HP == 64 ? kCap64 : 32) / side_tpc(side); }
 __host__ __device__ constexpr int side_nt(int HP, int side) { return HP / 2 * side_tpc(side); }
 
-// slot tables inside the caller's workspace (see sparse_tables_bytes)
+// slot tables inside the caller's workspace (see sparse_tables_bytes): neuron
+// assignments and synapse lists only; the kernels read each slot's constants from
+// the dense gate pack (pack[p][q]) once at start, so the tables depend on the
+// nonzero pattern alone
 struct SlotTablesView {
   int* fneu;      // [HP]          neuron of (pair c, r) at 2c + r (forward: column q)
   int* fk;        // [warps]       K1 | K2 << 8
-  float4* fpack;  // [NTf][2][KMf] (sigma/2, -sigma*mu/2, w_pos/2, w_erev/2)
   int* fidx;      // [NTf][2][KMf] presynaptic neuron p, -1 = padding
   int* bneu;      // [HP]          backward: row p
   int* bk;        // [warps]
-  float4* bpack;  // [NTb][2][KMb] (-sigma/2, sigma*mu/2, w_pos, w_erev)
   int* bidx;      // [NTb][2][KMb] postsynaptic neuron q, -1 = padding
   int* overflow;  // [1]           1 if a neuron has more nonzero synapses than the capacity
 };
@@ -67,13 +69,12 @@ struct SlotTablesView {
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
 // byte offsets of the table arrays; returns the total size
-inline size_t tables_layout(int HP, size_t (&at)[9]) {
+inline size_t tables_layout(int HP, size_t (&at)[7]) {
   const size_t nf = (size_t)side_nt(HP, 1) * 2 * side_km(HP, 1), nb = (size_t)side_nt(HP, 0) * 2 * side_km(HP, 0);
-  const size_t sz[9] = {HP * sizeof(int), side_nt(HP, 1) / 32 * sizeof(int), nf * sizeof(float4), nf * sizeof(int),
-                        HP * sizeof(int), side_nt(HP, 0) / 32 * sizeof(int), nb * sizeof(float4), nb * sizeof(int),
-                        sizeof(int)};
+  const size_t sz[7] = {HP * sizeof(int), side_nt(HP, 1) / 32 * sizeof(int), nf * sizeof(int), HP * sizeof(int),
+                        side_nt(HP, 0) / 32 * sizeof(int), nb * sizeof(int), sizeof(int)};
   size_t o = 0;
-  for (int i = 0; i < 9; ++i) {
+  for (int i = 0; i < 7; ++i) {
     at[i] = o;
     o = align_up(o + sz[i]);
   }
@@ -82,18 +83,16 @@ inline size_t tables_layout(int HP, size_t (&at)[9]) {
 
 inline SlotTablesView tables_view(void* base, int HP) {
   char* b = static_cast<char*>(base);
-  size_t at[9];
+  size_t at[7];
   tables_layout(HP, at);
   SlotTablesView v;
   v.fneu = reinterpret_cast<int*>(b + at[0]);
   v.fk = reinterpret_cast<int*>(b + at[1]);
-  v.fpack = reinterpret_cast<float4*>(b + at[2]);
-  v.fidx = reinterpret_cast<int*>(b + at[3]);
-  v.bneu = reinterpret_cast<int*>(b + at[4]);
-  v.bk = reinterpret_cast<int*>(b + at[5]);
-  v.bpack = reinterpret_cast<float4*>(b + at[6]);
-  v.bidx = reinterpret_cast<int*>(b + at[7]);
-  v.overflow = reinterpret_cast<int*>(b + at[8]);
+  v.fidx = reinterpret_cast<int*>(b + at[2]);
+  v.bneu = reinterpret_cast<int*>(b + at[3]);
+  v.bk = reinterpret_cast<int*>(b + at[4]);
+  v.bidx = reinterpret_cast<int*>(b + at[5]);
+  v.overflow = reinterpret_cast<int*>(b + at[6]);
   return v;
 }
 
@@ -102,25 +101,28 @@ inline SlotTablesView tables_view(void* base, int HP) {
 // column q, list = its nonzero rows p.
 template <int HP>
 __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, const float* __restrict__ w_pos,
-                                                          const float* __restrict__ w_erev,
-                                                          const float* __restrict__ sigma,
-                                                          const float* __restrict__ mu, int H) {
+                                                          const float* __restrict__ w_erev, int H) {
   constexpr int NPAIR = HP / 2, CAP = HP == 64 ? kCap64 : 32;
   __shared__ uint64_t nz[2][HP];  // [0] bit q of row p; [1] bit p of column q
   __shared__ int cnt[2][HP];
   __shared__ int order[2][HP];    // neurons by count, descending
+  __shared__ unsigned char lst[2][HP][HP];  // each neuron's list (neuron indices), in emission order
   const int tid = threadIdx.x;
-  for (int p = tid; p < HP; p += blockDim.x) {
+  // nonzero pattern: one warp per row, a ballot per 32 columns (coalesced loads, no atomics)
+  const int warp = tid / 32, lane = tid % 32, nwarps = blockDim.x / 32;
+  for (int p = warp; p < HP; p += nwarps) {
     uint64_t m = 0;
-    if (p < H)
-      for (int q = 0; q < H; ++q) {
-        const long long j = (long long)p * H + q;
-        if (w_pos[j] != 0.f || w_erev[j] != 0.f) m |= 1ull << q;
-      }
-    nz[0][p] = m;
-    cnt[0][p] = __popcll(m);
+#pragma unroll
+    for (int h = 0; h < HP / 32; ++h) {
+      const int q = 32 * h + lane;
+      const long long j = (long long)p * H + q;
+      const bool on = p < H && q < H && (w_pos[j] != 0.f || w_erev[j] != 0.f);
+      m |= (uint64_t)__ballot_sync(0xffffffffu, on) << (32 * h);
+    }
+    if (lane == 0) nz[0][p] = m;
   }
   __syncthreads();
+  for (int p = tid; p < HP; p += blockDim.x) cnt[0][p] = __popcll(nz[0][p]);
   for (int q = tid; q < HP; q += blockDim.x) {
     uint64_t m = 0;
     for (int p = 0; p < HP; ++p)
@@ -157,40 +159,42 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
       (s ? tv.fk : tv.bk)[w] = k1 | (k2 << 8);
     }
   }
-  // lists: one thread per (side, pair, r); entries round-robin over residues mod 8
-  for (int i = tid; i < 2 * HP; i += blockDim.x) {
-    const int s = i / HP, k = i % HP, c = k / 2, r = k % 2;
-    const int n = order[s][r ? HP - 1 - c : c];
+  // lists: a neuron's nonzero partners in round-robin order over the residues mod 8
+  // (round k takes the k-th partner of every residue class, classes in order); each
+  // partner's position follows from the class counts, so all entries are placed in
+  // parallel
+  constexpr uint64_t kClass0 = 0x0101010101010101ull;  // partners o with o % 8 == 0
+  __shared__ int ccount[2][HP][8];
+  for (int i = tid; i < 2 * HP * 8; i += blockDim.x) {
+    const int s = i / (HP * 8), n = (i / 8) % HP, b = i % 8;
+    ccount[s][n][b] = __popcll(nz[s][n] & (kClass0 << b));
+  }
+  __syncthreads();
+  for (int i = tid; i < 2 * HP * HP; i += blockDim.x) {
+    const int s = i / (HP * HP), n = (i / HP) % HP, o = i % HP;
     const uint64_t m = nz[s][n];
-    float4* pk = s ? tv.fpack : tv.bpack;
-    int* ix = s ? tv.fidx : tv.bidx;
-    const int TPC = side_tpc(s), KM = side_km(HP, s);
-    int next[8];
+    if (!((m >> o) & 1ull)) continue;
+    const int b = o & 7;
+    const int k = __popcll(m & (kClass0 << b) & ((1ull << o) - 1ull));  // rank within its class
+    int pos = 0;
 #pragma unroll
-    for (int b = 0; b < 8; ++b) next[b] = b;
-    int e = 0;
-    const int total = min(__popcll(m), TPC * KM);
-    while (e < total) {
-      for (int b = 0; b < 8 && e < total; ++b) {
-        int o = next[b];
-        while (o < HP && !((m >> o) & 1ull)) o += 8;
-        if (o >= HP) continue;
-        next[b] = o + 8;
-        const int p = s ? o : n, q = s ? n : o;  // synapse (p, q)
-        const long long j = (long long)p * H + q;
-        const float sg = sigma[j], wp = w_pos[j], we = w_erev[j];
-        const int slot = ((c * TPC + e % TPC) * 2 + r) * KM + e / TPC;
-        pk[slot] = s ? make_float4(0.5f * sg, -0.5f * sg * mu[j], 0.5f * wp, 0.5f * we)
-                     : make_float4(-0.5f * sg, 0.5f * sg * mu[j], wp, we);
-        ix[slot] = o;
-        ++e;
-      }
+    for (int bb = 0; bb < 8; ++bb) {
+      const int cb = ccount[s][n][bb];
+      pos += min(cb, k) + ((bb < b && cb > k) ? 1 : 0);
     }
-    for (; e < TPC * KM; ++e) {
-      const int slot = ((c * TPC + e % TPC) * 2 + r) * KM + e / TPC;
-      pk[slot] = make_float4(0.f, 0.f, 0.f, 0.f);
-      ix[slot] = -1;
-    }
+    lst[s][n][pos] = (unsigned char)o;
+  }
+  __syncthreads();
+  // ... then every thread fills slots of both tables in parallel
+  constexpr int NF = side_nt(HP, 1) * 2 * side_km(HP, 1), NB = side_nt(HP, 0) * 2 * side_km(HP, 0);
+  for (int i = tid; i < NF + NB; i += blockDim.x) {
+    const int s = i < NF ? 1 : 0;
+    const int slot = s ? i : i - NF;
+    const int TPC = side_tpc(s), KM = side_km(HP, s);
+    const int j = slot % KM, r = (slot / KM) % 2, t = slot / (2 * KM);
+    const int c = t / TPC, e = j * TPC + t % TPC;
+    const int n = order[s][r ? HP - 1 - c : c];
+    (s ? tv.fidx : tv.bidx)[slot] = e < min(cnt[s][n], TPC * KM) ? lst[s][n][e] : -1;
   }
 }
 
@@ -322,8 +326,10 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int base = (tid * 2 + r) * KM + j;
-      const float4 pk = tv.fpack[base];
-      const int ix = tv.fidx[base];
+      const int ix = tv.fidx[base];  // presynaptic neuron; the constants come from the dense pack
+      float4 pk = ix < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : a.pack[(long long)ix * HP + tv.fneu[2 * c + r]];
+      pk.z *= 0.5f;
+      pk.w *= 0.5f;
       f.sl2[r][j] = make_float2(pk.x, pk.x);
       f.nm2[r][j] = make_float2(pk.y, pk.y);
       f.wp2[r][j] = make_float2(pk.z, pk.z);
@@ -489,8 +495,10 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int base = (tid * 2 + r) * KM + j;
-      const float4 pk = tv.bpack[base];
-      const int ix = tv.bidx[base];
+      const int ix = tv.bidx[base];  // postsynaptic neuron; the constants come from the dense pack
+      float4 pk = ix < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : a.pack[(long long)(r ? rowB : rowA) * HP + ix];
+      pk.x = -pk.x;  // negated half-scale constants: the gate argument is -z/2
+      pk.y = -pk.y;
       f.sl2[r][j] = make_float2(pk.x, pk.x);
       f.nm2[r][j] = make_float2(pk.y, pk.y);
       f.wp2[r][j] = make_float2(pk.z, pk.z);
@@ -680,7 +688,7 @@ cudaError_t launch_plain(K kernel, const Args& a, const SlotTablesView& tv, int 
 }  // namespace
 
 size_t sparse_tables_bytes(int HP) {
-  size_t at[9];
+  size_t at[7];
   return tables_layout(HP, at);
 }
 
@@ -719,9 +727,9 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
 cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st) {
   const SlotTablesView tv = tables_view(tables, pa.HP);
   if (pa.HP == 64)
-    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.sigma, pa.mu, pa.H);
+    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H);
   else
-    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.sigma, pa.mu, pa.H);
+    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H);
   return cudaGetLastError();
 }
 
