@@ -300,9 +300,11 @@ def module_parity(run_ours, make_ours, ltc, p, cfg, dev):
             "pass": bool(fwd < 1e-3 and ok), "against": "reference ltc.py TorchScript path on the GPU"}
 
 
-def rec_synapses(model, cfg) -> int:
+def rec_synapses(model, cfg, rows) -> int:
     """Recurrent synapses per unfold the kernels visit (see ltc_cuda.skip_zero_synapses)."""
-    if getattr(model, "skip_zero_synapses", False) and cfg.H <= 64 and model._skip_fits():
+    import ltc_layer
+    if (getattr(model, "skip_zero_synapses", False) and cfg.H <= 64 and model._skip_fits()
+            and rows >= ltc_layer.SKIP_MIN_ROWS):
         return int(model.sparsity_mask.count_nonzero().item())
     return cfg.H * cfg.H
 
@@ -563,7 +565,7 @@ def main():
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     # recurrent synapses the kernels visit: the nonzero ones when the module lets the
     # solver skip masked synapses (H <= 64), else all H*H
-    rec_syn = rec_synapses(model, cfg)
+    rec_syn = rec_synapses(model, cfg, Bl * cfg.T)
     visits = {"recurrent_fwd": Bl * cfg.T * cfg.U * rec_syn,
               "recurrent_bwd": Bl * cfg.T * cfg.U * rec_syn,
               "sensory_fwd": Bl * cfg.T * cfg.D * cfg.H,

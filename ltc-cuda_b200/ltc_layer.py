@@ -23,6 +23,11 @@ import ltc_cuda
 # host logic (e.g. multi-process data parallel) on machines without a GPU.
 _solver: Callable = ltc_cuda.ltc_cuda_forward
 
+# B*T below which the module keeps the dense recurrent kernels even when it may skip
+# masked synapses: the per-call slot-table build (tens of microseconds) outweighs the
+# saving there (measured on B200: c0/c1, B*T = 192/512, are faster dense)
+SKIP_MIN_ROWS = 4096
+
 
 def set_solver(fn: Optional[Callable]) -> None:
     global _solver
@@ -126,7 +131,9 @@ class TrueLiquidTimeConstant(nn.Module):
                                f"(got {x.dtype} on {x.device}); there is no CPU fallback")
         # w_pos = softplus(w) * mask: the solver's gradients at masked synapses are
         # multiplied by zero on the way to w and erev, so the solver may skip them
-        with ltc_cuda.skip_zero_synapses(self.skip_zero_synapses and self._skip_fits()):
+        # (small problems stay dense: rebuilding the slot tables costs more than it saves)
+        skip = self.skip_zero_synapses and B * T >= SKIP_MIN_ROWS and self._skip_fits()
+        with ltc_cuda.skip_zero_synapses(skip):
             outputs, state = _solver(x, state, w_pos, w_erev, self.mu, self.sigma, self.sensory_mu,
                                      self.sensory_sigma, self.sensory_erev, sensory_w_pos, cm_t, gleak_pos,
                                      self.vleak, self.ode_unfolds, self.epsilon)
