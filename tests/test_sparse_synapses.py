@@ -180,7 +180,7 @@ def test_module_grads_match_dense_path():
     torch.manual_seed(4)
     m = ltc_layer.TrueLiquidTimeConstant(40, 64, sparsity=0.4).cuda()
     assert m.skip_zero_synapses
-    x = torch.randn(7, 10, 40, device="cuda")
+    x = torch.randn(128, 40, 40, device="cuda")  # B*T above ltc_layer.SKIP_MIN_ROWS
     grads = []
     for skip in (True, False):
         m.skip_zero_synapses = skip
