@@ -59,7 +59,7 @@ def parse():
     ap.add_argument("--lean", type=int, default=0,
                     help="1: memory-lean training (step-boundary states saved, unfolds recomputed in the backward)")
     ap.add_argument("--skip-zero", type=int, default=1,
-                    help="1 (default): the module lets the solver skip masked recurrent synapses (H <= 64); 0: dense")
+                    help="1 (default): the module lets the solver skip masked recurrent synapses (H <= 64 and 128 < H <= 512); 0: dense")
     ap.add_argument("--graph", type=int, default=None,
                     help="1 (default): replay the whole step as a captured CUDA graph; 0: eager launches")
     return ap.parse_args()
@@ -303,7 +303,7 @@ def module_parity(run_ours, make_ours, ltc, p, cfg, dev):
 def rec_synapses(model, cfg, rows) -> int:
     """Recurrent synapses per unfold the kernels visit (see ltc_cuda.skip_zero_synapses)."""
     import ltc_layer
-    if (getattr(model, "skip_zero_synapses", False) and cfg.H <= 64 and model._skip_fits()
+    if (getattr(model, "skip_zero_synapses", False) and (cfg.H <= 64 or cfg.H > 128) and model._skip_fits()
             and rows >= ltc_layer.SKIP_MIN_ROWS):
         return int(model.sparsity_mask.count_nonzero().item())
     return cfg.H * cfg.H
@@ -564,7 +564,7 @@ def main():
     f_mhz = float(peaks.get("sm_max_mhz", 1965.0))
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     # recurrent synapses the kernels visit: the nonzero ones when the module lets the
-    # solver skip masked synapses (H <= 64), else all H*H
+    # solver skip masked synapses (H <= 64 or 128 < H <= 512), else all H*H
     rec_syn = rec_synapses(model, cfg, Bl * cfg.T)
     visits = {"recurrent_fwd": Bl * cfg.T * cfg.U * rec_syn,
               "recurrent_bwd": Bl * cfg.T * cfg.U * rec_syn,

@@ -51,10 +51,13 @@ typedef struct {
  * whenever w_pos = softplus(w) * mask, since the chain rule multiplies them by the
  * mask -- and the solver visits only the nonzero synapses; the four recurrent
  * gradients (w_pos, w_erev, mu, sigma) are written as zero at the skipped
- * positions.  Every other output is unchanged.  Honoured for H <= 64 (other sizes
- * run the dense kernels); the slot tables are rebuilt on the device at every call.
- * Capacity: for 32 < H <= 64 every neuron may have at most 48 nonzero incoming and
- * 48 nonzero outgoing synapses (any pattern fits for H <= 32).  The library cannot
+ * positions.  Every other output is unchanged.  Honoured for H <= 64 and for
+ * 128 < H <= 512 (64 < H <= 128 runs the dense kernels); the synapse tables are
+ * rebuilt on the device at every call.  Capacity: for 32 < H <= 64 every neuron may
+ * have at most 48 nonzero incoming and 48 nonzero outgoing synapses (any pattern
+ * fits for H <= 32); for 128 < H <= 512 at most 128 nonzero synapses leave each
+ * neuron and at most 8192 enter each block of HP/8 consecutive neurons (HP = 256
+ * for H <= 256, else 512).  The library cannot
  * report a violation without a device sync, so a call that exceeds it writes NaN
  * to its outputs and gradients; check the pattern before setting the flag. */
 #define LTC_FLAG_SKIP_ZERO_SYNAPSES 4

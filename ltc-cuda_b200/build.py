@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libltc_sm100.so")
 SOURCES = ["ltc_capi.cu", "ltc_prep.cu", "ltc_sensory.cu", "ltc_recurrent.cu", "ltc_recurrent_wide.cu",
-           "ltc_noalloc.cu", "ltc_recurrent_stream.cu", "ltc_recurrent_sparse.cu",
+           "ltc_noalloc.cu", "ltc_recurrent_stream.cu", "ltc_recurrent_sparse.cu", "ltc_recurrent_csparse.cu",
            "ltc_preamble.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

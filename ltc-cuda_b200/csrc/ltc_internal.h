@@ -110,7 +110,8 @@ struct RecPlan {
   bool wide;       // not the register-resident kernels (streamed or generic wide-H)
   bool streamed;   // cluster-streamed kernels (128 < H <= 512)
   bool tanh_space; // synapse partials hold sum a'*tanh (a' = -a/4); partn has 5 rows (+ sum a_n, sum a_d)
-  bool sparse;     // zero synapses skipped (LTC_FLAG_SKIP_ZERO_SYNAPSES, H <= 64): slot-table kernels
+  bool sparse;     // zero synapses skipped (LTC_FLAG_SKIP_ZERO_SYNAPSES): slot-table kernels (H <= 64) or
+                   // cluster list kernels (128 < H <= 512, with streamed set)
   size_t scratch_fwd, scratch_bwd;  // floats of path-specific global scratch
   int HP;          // padded neuron count
   int ns_fwd, grid_fwd, threads_fwd;
@@ -127,6 +128,12 @@ void plan_sparse(RecPlan& p, int B, int num_sms);
 cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st);
 cudaError_t launch_sparse_fwd(const RecFwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st);
 cudaError_t launch_sparse_bwd(const RecBwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st);
+// 128 < H <= 512 (ltc_recurrent_csparse.cu; reached through the calls above)
+size_t csp_tables_bytes(int HP);
+void plan_csparse(RecPlan& p, int B, int num_clusters);
+cudaError_t launch_build_csp(const PackArgs& pa, void* tables, cudaStream_t st);
+cudaError_t launch_csp_fwd(const RecFwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st);
+cudaError_t launch_csp_bwd(const RecBwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st);
 // chunk width of the streamed backward (256 threads, 8-CTA clusters), 0 on other paths
 inline int stream_chunk_cols(const RecPlan& p) { return p.streamed ? 16384 / p.HP : 0; }
 cudaError_t launch_recurrent_fwd(const RecFwdArgs& a, const RecPlan& p, cudaStream_t st);

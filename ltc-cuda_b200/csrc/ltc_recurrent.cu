@@ -680,6 +680,11 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide, bool skip_zero
     plan_sparse(p, B, num_sms);
     return p;
   }
+  if (skip_zero && !force_wide && H > 128) {
+    p.HP = H <= 256 ? 256 : 512;
+    plan_csparse(p, B, resident_clusters(8, num_sms));
+    return p;
+  }
   if (force_wide) {
     p.wide = true;
     plan_wide(p, B, H, num_sms);

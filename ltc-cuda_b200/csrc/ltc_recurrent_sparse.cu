@@ -688,6 +688,7 @@ cudaError_t launch_plain(K kernel, const Args& a, const SlotTablesView& tv, int 
 }  // namespace
 
 size_t sparse_tables_bytes(int HP) {
+  if (HP > 64) return csp_tables_bytes(HP);
   size_t at[7];
   return tables_layout(HP, at);
 }
@@ -725,6 +726,7 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
 }
 
 cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st) {
+  if (pa.HP > 64) return launch_build_csp(pa, tables, st);
   const SlotTablesView tv = tables_view(tables, pa.HP);
   if (pa.HP == 64)
     build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H);
@@ -734,12 +736,14 @@ cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st
 }
 
 cudaError_t launch_sparse_fwd(const RecFwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st) {
+  if (p.streamed) return launch_csp_fwd(a, p, tables, st);
   const SlotTablesView tv = tables_view(const_cast<void*>(tables), p.HP);
   return p.HP == 64 ? launch_plain(rec_fwd_sparse<64>, a, tv, p.grid_fwd, p.threads_fwd, p.smem_fwd, st)
                     : launch_plain(rec_fwd_sparse<32>, a, tv, p.grid_fwd, p.threads_fwd, p.smem_fwd, st);
 }
 
 cudaError_t launch_sparse_bwd(const RecBwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st) {
+  if (p.streamed) return launch_csp_bwd(a, p, tables, st);
   const SlotTablesView tv = tables_view(const_cast<void*>(tables), p.HP);
   return p.HP == 64 ? launch_plain(rec_bwd_sparse<64>, a, tv, p.grid_bwd, p.threads_bwd, p.smem_bwd, st)
                     : launch_plain(rec_bwd_sparse<32>, a, tv, p.grid_bwd, p.threads_bwd, p.smem_bwd, st);

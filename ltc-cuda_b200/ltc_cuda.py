@@ -212,21 +212,44 @@ class skip_zero_synapses:
         return False
 
 
-# The synapse-skipping kernels hold at most this many nonzero synapses per neuron
-# (incoming and outgoing) for 32 < H <= 64; for H <= 32 any mask fits.  A call that
-# exceeds it gets NaN outputs from the kernels, so callers check first.
+# Capacity of the synapse-skipping kernels.  32 < H <= 64: at most this many nonzero
+# synapses per neuron (incoming and outgoing); H <= 32: any mask.  128 < H <= 512
+# (HP = 256 or 512 padded neurons, 8 blocks of HP/8): at most 8192 nonzero synapses
+# enter each block, and inside each block the rows, ranked by outgoing count and
+# paired c-th heaviest with c-th lightest in warps of 4 pairs, need
+# 4*ceil(max ceil(heavy/8)/4) + 4*ceil(max ceil(light/8)/4) <= 32 slots per warp.
+# 64 < H <= 128 runs dense kernels (the flag is ignored).  A call beyond the capacity
+# gets NaN outputs from the kernels, so callers check first.
 SKIP_MAX_SYNAPSES_PER_NEURON = 48
+SKIP_WIDE_MAX_PER_BLOCK = 8192
+SKIP_WIDE_SLOTS_PER_LANE = 32
+
+
+def _wide_fits(nz: torch.Tensor) -> bool:
+    H = nz.shape[0]
+    HP = 256 if H <= 256 else 512
+    NEUR = HP // 8
+    pad = torch.zeros(HP, HP, dtype=torch.bool, device=nz.device)
+    pad[:H, :H] = nz
+    if int(pad.sum(0).view(8, NEUR).sum(1).max().item()) > SKIP_WIDE_MAX_PER_BLOCK:
+        return False
+    rows = pad.sum(1).view(8, NEUR).sort(dim=1, descending=True).values  # per block, heaviest first
+    heavy = (rows[:, :NEUR // 2] + 7) // 8
+    light = (rows.flip(1)[:, :NEUR // 2] + 7) // 8
+    k1 = (heavy.view(8, -1, 4).max(2).values + 3) // 4 * 4
+    k2 = (light.view(8, -1, 4).max(2).values + 3) // 4 * 4
+    return int((k1 + k2).max().item()) <= SKIP_WIDE_SLOTS_PER_LANE
 
 
 def skip_zero_synapses_fits(mask: torch.Tensor) -> bool:
     """True when the (H, H) nonzero pattern ``mask`` fits the synapse-skipping kernels."""
     H = mask.shape[0]
-    if H > 64:
-        return True  # the flag is ignored above H = 64 (dense kernels run)
-    if H <= 32:
-        return True
     nz = mask != 0
-    return int(torch.maximum(nz.sum(0).max(), nz.sum(1).max()).item()) <= SKIP_MAX_SYNAPSES_PER_NEURON
+    if H <= 32 or 64 < H <= 128:
+        return True
+    if H <= 64:
+        return int(torch.maximum(nz.sum(0).max(), nz.sum(1).max()).item()) <= SKIP_MAX_SYNAPSES_PER_NEURON
+    return _wide_fits(nz)
 
 
 def _call_flags_now() -> int:
