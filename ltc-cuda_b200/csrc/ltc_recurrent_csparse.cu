@@ -414,8 +414,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
   float4* cst = reinterpret_cast<float4*>(smem);                     // [kBK][kNT]
   float* anc = smem + 4 * kBK * kNT;                                   // [HP][4 * kCS4]
   float* adc = anc + HP * 4 * kCS4;                                    // [HP][4 * kCS4]
-  float* vpc = adc + HP * 4 * kCS4;                                    // [NEUR][kCS]  V[n] of the own rows
-  uint16_t* qix = reinterpret_cast<uint16_t*>(vpc + NEUR * kCS);      // [kBK][kNT]
+  // per chunk, double-buffered: V[n], V[n-1], R[n-1], DIR, GSN, GSD of the own rows
+  float* tdat = adc + HP * 4 * kCS4;                                   // [2][6][NEUR][kCS]
+  uint16_t* qix = reinterpret_cast<uint16_t*>(tdat + 2 * 6 * NEUR * kCS);  // [kBK][kNT]
   float* dvb = reinterpret_cast<float*>(qix + kBK * kNT);              // [NEUR][kCS]  dL/dv of the chunk
   int* rowof = reinterpret_cast<int*>(dvb + NEUR * kCS);               // [NEUR]  row of slot 2c + r
 
@@ -471,7 +472,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
   const int own = LR::own_base(lane);  // item (row own / 4, sample own % 4) of a block
 
   // prep of unfold m for (sample bs, row rsel) given g = dL/dv_{m+1}
-  auto prep = [&](int rsel, int m, long long bs, float gval, bool first, float vin, float vout, float rr) {
+  auto prep = [&](int rsel, int m, long long bs, float gval, bool first, float vin, float vout, float rr,
+                  float gsn_prev, float gsd_prev) {
     const int p = prow(rsel);
     const float an = gval * rr;
     const float ad = -an * vout;
@@ -481,8 +483,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
     sums[rsel][3] += an;
     sums[rsel][4] += ad;
     const long long o = bs * HP + p;
-    GSNg[o] = first ? an : GSNg[o] + an;
-    GSDg[o] = first ? ad : GSDg[o] + ad;
+    GSNg[o] = first ? an : gsn_prev + an;
+    GSDg[o] = first ? ad : gsd_prev + ad;
     DIRg[o] = an * nrn2[rsel].x;
     ANg[(m & 1) * SV + (long long)p * BP + bs] = -0.25f * an;
     ADg[(m & 1) * SV + (long long)p * BP + bs] = -0.25f * ad;
@@ -500,7 +502,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
           if (a.gstate) gval += a.gstate[bs * H + p];
           const long long m = NTU - 1;
           prep(rsel, NTU - 1, bs, gval, true, a.V[(m * B + bs) * H + p], a.V[((m + 1) * B + bs) * H + p],
-               a.R[(m * B + bs) * H + p]);
+               a.R[(m * B + bs) * H + p], 0.f, 0.f);
         } else {
           for (int par = 0; par < 2; ++par) {
             ANg[par * SV + (long long)p * BP + bs] = 0.f;
@@ -518,20 +520,39 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
     const float* ANn = ANg + (n & 1) * SV;
     const float* ADn = ADg + (n & 1) * SV;
     const bool last = (k == 0 && t == 0);
-    for (int ch = 0; ch < nch; ++ch) {
-      const int sc = ch * kCS;  // first sample of the chunk (in the group)
+    // staging of chunk ch into the adjoint buffers (free while no pass runs) and
+    // tail buffer tb_: everything the chunk's pass and tails read, so the tails
+    // wait on no global load
+    auto stage = [&](int ch, int tbuf) {
+      const int sc = ch * kCS;
       for (int i = tid; i < HP * (kCS / 4); i += kNT) {
         const int q = i / (kCS / 4), k4 = i % (kCS / 4);
         cp_async16(anc + q * 4 * kCS4 + 4 * k4, ANn + (long long)q * BP + b0 + sc + 4 * k4);
         cp_async16(adc + q * 4 * kCS4 + 4 * k4, ADn + (long long)q * BP + b0 + sc + 4 * k4);
       }
-      for (int i = tid; i < NEUR * kCS; i += kNT) {
-        const int rs = i / kCS, s = i % kCS;
+      float* td = tdat + tbuf * 6 * NEUR * kCS;
+      for (int i = tid; i < 6 * NEUR * kCS; i += kNT) {
+        const int fld = i / (NEUR * kCS), rs = (i / kCS) % NEUR, sl = i % kCS;
         const int row = rowof[rs];
-        const bool ok = sc + s < nvalid && row < H;
-        cp_async4_zfill(vpc + i, a.V + ((long long)n * B + b0 + (ok ? sc + s : 0)) * H + (ok ? row : 0), ok);
+        const long long bs = b0 + sc + sl;
+        const bool ok = sc + sl < nvalid && row < H && (fld == 0 || fld >= 3 || !last);
+        const float* src;
+        switch (fld) {
+          case 0: src = a.V + ((long long)n * B + bs) * H + row; break;
+          case 1: src = a.V + ((long long)(n - 1) * B + bs) * H + row; break;
+          case 2: src = a.R + ((long long)(n - 1) * B + bs) * H + row; break;
+          case 3: src = DIRg + bs * HP + row; break;
+          case 4: src = GSNg + bs * HP + row; break;
+          default: src = GSDg + bs * HP + row; break;
+        }
+        cp_async4_zfill(td + i, ok ? src : a.V, ok);
       }
       cp_async_commit();
+    };
+    stage(0, 0);
+    for (int ch = 0; ch < nch; ++ch) {
+      const int sc = ch * kCS;  // first sample of the chunk (in the group)
+      const float* td = tdat + (ch & 1) * 6 * NEUR * kCS;
       cp_async_wait_all();
       __syncthreads();
       if (sc + kCS > nvalid) {  // samples past the group's last: their adjoints must not count
@@ -548,7 +569,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
         float4 vr[2];
 #pragma unroll
         for (int rsel = 0; rsel < 2; ++rsel)
-          vr[rsel] = active ? *reinterpret_cast<const float4*>(vpc + (2 * c + rsel) * kCS + blk * kSB)
+          vr[rsel] = active ? *reinterpret_cast<const float4*>(td + (2 * c + rsel) * kCS + blk * kSB)
                             : make_float4(0.f, 0.f, 0.f, 0.f);
         const float* an_b = anc + blk * kSB;
         const float* ad_b = adc + blk * kSB;
@@ -558,47 +579,39 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
         LR::template run<1>(acc, lane);
         if (active) dvb[(2 * c + own / kSB) * kCS + blk * kSB + own % kSB] = acc[0][0];
       }
-      __syncthreads();
+      __syncthreads();  // adjoint buffers free: the next chunk streams in behind the tails
+      if (ch + 1 < nch) stage(ch + 1, (ch + 1) & 1);
       // tails of the chunk: lane l takes sample sc + l of both rows
       if (active) {
         const int s = sc + l;
         const long long bs = b0 + s;
-        float dirv[2], gsnv[2], gsdv[2], rv[2], gov[2], vinv[2];
+        float gov[2] = {0.f, 0.f};
 #pragma unroll
         for (int rsel = 0; rsel < 2; ++rsel) {
           const int p = prow(rsel);
-          dirv[rsel] = gsnv[rsel] = gsdv[rsel] = rv[rsel] = gov[rsel] = vinv[rsel] = 0.f;
-          if (s < nvalid && p < H) {
-            const long long o = bs * HP + p;
-            dirv[rsel] = __ldcg(DIRg + o);
-            gsnv[rsel] = __ldcg(GSNg + o);
-            gsdv[rsel] = __ldcg(GSDg + o);
-            if (!last) {
-              rv[rsel] = a.R[((long long)(n - 1) * B + bs) * H + p];
-              vinv[rsel] = a.V[((long long)(n - 1) * B + bs) * H + p];
-              if (k == 0) gov[rsel] = a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
-            }
-          }
+          if (s < nvalid && p < H && !last && k == 0)
+            gov[rsel] = a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
         }
 #pragma unroll
         for (int rsel = 0; rsel < 2; ++rsel) {
           const int p = prow(rsel);
           if (s >= nvalid || p >= H) continue;
-          float gval = fmaf(-2.0f, dvb[(2 * c + rsel) * kCS + l], dirv[rsel]);  // constants hold -sigma/2
+          const int ti = (2 * c + rsel) * kCS + l;
+          const float dirv = td[3 * NEUR * kCS + ti], gsnv = td[4 * NEUR * kCS + ti], gsdv = td[5 * NEUR * kCS + ti];
+          float gval = fmaf(-2.0f, dvb[ti], dirv);  // the constants hold -sigma/2
           if (k == 0) {
             const long long row = bs * T + t;
-            a.gsn[row * H + p] = gsnv[rsel];
-            a.gsd[row * H + p] = gsdv[rsel];
+            a.gsn[row * H + p] = gsnv;
+            a.gsd[row * H + p] = gsdv;
             if (last) {
               a.gh0[bs * H + p] = gval;
               continue;
             }
             gval += gov[rsel];
           }
-          prep(rsel, n - 1, bs, gval, k == 0, vinv[rsel], vpc[(2 * c + rsel) * kCS + l], rv[rsel]);
+          prep(rsel, n - 1, bs, gval, k == 0, td[NEUR * kCS + ti], td[ti], td[2 * NEUR * kCS + ti], gsnv, gsdv);
         }
       }
-      __syncthreads();  // the chunk buffers are restaged next
     }
     cluster.sync();  // release a'_n / a'_d of unfold n-1 / acquire the peers'
     if (--k < 0) {
@@ -692,7 +705,7 @@ void plan_csparse(RecPlan& p, int B, int num_clusters) {
   p.threads_fwd = p.threads_bwd = kNT;
   p.slots_bwd = p.grid_bwd / kCL;
   p.smem_fwd = (size_t)kFCap * 16 + (size_t)HP * kFS * 4 + (size_t)kFCap * 2 + (NEUR + 1) * 4 + 2 * NEUR * 4;
-  p.smem_bwd = (size_t)kBK * kNT * 16 + (size_t)2 * HP * 4 * kCS4 * 4 + (size_t)NEUR * kCS * 4 +
+  p.smem_bwd = (size_t)kBK * kNT * 16 + (size_t)2 * HP * 4 * kCS4 * 4 + (size_t)2 * 6 * NEUR * kCS * 4 +
                (size_t)kBK * kNT * 2 + (size_t)NEUR * kCS * 4 + NEUR * 4;
   p.tanh_space = true;
   const size_t BP = (size_t)(p.grid_fwd / kCL) * ns + kFS;
