@@ -33,10 +33,12 @@ import torch.distributed as dist  # noqa: E402
 import synth  # noqa: E402
 
 # DRAM bytes per (sample, timestep) of a kernel from one ncu capture of a smaller case
-# of the same configuration (c3 shape at B=1184: dram__bytes_read + dram__bytes_write
-# = 466.5 + 70.4 MB over 1184*128 (b,t)), scaled to a launch by the (b,t) units it
-# processes (the traffic is the saved V/R read and the g_sn/g_sd write, linear in B).
-NCU_TRAFFIC_PER_BT = {("c3", "recurrent_bwd"): 3543.0}
+# of the same configuration, scaled to a launch by the (b,t) units it processes (the
+# traffic is the saved V/R read and the g_sn/g_sd write, linear in B and T): c3 shape
+# at B=1184 (dram__bytes_read + dram__bytes_write = 466.8 + 69.9 MB over 1184*128
+# (b,t)); c4 at T=4 (246.5 + 57.2 MB over 1024*4 (b,t)).  Both with masked synapses
+# skipped (the bench default).
+NCU_TRAFFIC_PER_BT = {("c3", "recurrent_bwd"): 3541.0, ("c4", "recurrent_bwd"): 74136.0}
 
 METRIC = "fwd+bwd sequence-timesteps/sec (B·T/s) at 1/2/4/8 B200; % FP32 roofline"
 UNIT = "B*T/s"
@@ -58,6 +60,8 @@ def parse():
     ap.add_argument("--seq", type=int, default=None, help="override the sequence length T (profiling captures)")
     ap.add_argument("--lean", type=int, default=0,
                     help="1: memory-lean training (step-boundary states saved, unfolds recomputed in the backward)")
+    ap.add_argument("--parity", type=int, default=1,
+                    help="1 (default): check a slice against the reference before timing; 0: skip (profiling)")
     ap.add_argument("--skip-zero", type=int, default=1,
                     help="1 (default): the module lets the solver skip masked recurrent synapses (H <= 64 and 128 < H <= 512); 0: dense")
     ap.add_argument("--graph", type=int, default=None,
@@ -441,7 +445,7 @@ def main():
         return float(t.item())
 
     parity = None
-    if rank == 0:
+    if rank == 0 and args.parity:
         parity = our_parity(cfg, p, dev)
     for _ in range(max(3, args.warmup)):
         step(x_dev)
