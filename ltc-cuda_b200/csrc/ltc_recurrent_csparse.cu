@@ -15,7 +15,8 @@
 // walked in lockstep, so each synapse's constants are a shared-memory broadcast
 // and the presynaptic states v[p][lane] of the staged 32-sample slice are
 // conflict-free loads; each lane owns its (column, sample) sum, so no lane
-// reduction is needed.
+// reduction is needed.  A slice with <= 16 (<= 8) samples splits the list over 2
+// (4) lane parts instead of idling lanes, and combines them with shuffles.
 // Backward: 4 lanes share a row (64 rows x 4 = 256 threads at HP = 512); a lane
 // holds up to 32 of the row's synapses with their 4 gradient sums in registers for
 // the whole sequence and their constants in shared memory; samples come in chunks
@@ -41,7 +42,8 @@ namespace ltc {
 namespace {
 
 constexpr int kCL = 8;        // CTAs per cluster
-constexpr int kNT = 256;      // threads per CTA
+constexpr int kNT = 256;      // threads per CTA (backward)
+constexpr int kNTF = 512;     // threads per CTA (forward: 16 warps hide the list walk's latencies)
 constexpr int kFCap = 8192;   // forward: synapses per CTA (its column block)
 constexpr int kBK = 32;       // backward: synapses per lane (both rows of its pair)
 constexpr int kBL = 8;        // backward lanes per row pair
@@ -148,10 +150,15 @@ __global__ void __launch_bounds__(kNT) build_csp_kernel(CspTables tb, const floa
   }
   __syncthreads();
   constexpr int NPAIR = NEUR / 2, NWB = NPAIR / 4;  // pairs; warps holding pairs
+  // pair group g (4 rank-consecutive pairs) -> warp: with 8 warps, groups 2s and 2s+1
+  // (similar slot counts) share scheduler s (warps s and s + 4), so each scheduler runs
+  // at most a couple of the compile-time variants and their code stays in its cache
+  auto warp_of = [](int g) { return NWB == 8 ? ((g & 1) ? 4 + g / 2 : g / 2) : g; };
   __shared__ int k1w[8], k2w[8];
-  for (int w = tid; w < 8; w += kNT) {
+  for (int g = tid; g < 8; g += kNT) {
+    const int w = g < NWB ? warp_of(g) : g;
     int k1 = 0, k2 = 0;
-    for (int c = 4 * w; c < 4 * w + 4 && w < NWB; ++c) {
+    for (int c = 4 * g; c < 4 * g + 4 && g < NWB; ++c) {
       k1 = max(k1, (cnt[order[c]] + kBL - 1) / kBL);
       k2 = max(k2, (cnt[order[NEUR - 1 - c]] + kBL - 1) / kBL);
     }
@@ -166,7 +173,10 @@ __global__ void __launch_bounds__(kNT) build_csp_kernel(CspTables tb, const floa
     k2w[w] = k2;
     tb.bk[r * 8 + w] = k1 | (k2 << 8);
   }
-  for (int i = tid; i < NEUR; i += kNT) tb.brow[r * NEUR + i] = nb + order[(i & 1) ? NEUR - 1 - i / 2 : i / 2];
+  for (int i = tid; i < NEUR; i += kNT) {  // rows of pair slot ps = warp * 4 + c % 4
+    const int c = i / 2, ps = warp_of(c / 4) * 4 + c % 4;
+    tb.brow[r * NEUR + 2 * ps + (i & 1)] = nb + order[(i & 1) ? NEUR - 1 - c : c];
+  }
   __syncthreads();
   // entries: a row's partners round-robin over the residues mod 8 (bank spread of
   // the gathers); entry e of row A -> lane e % 8, slot e / 8; of row B -> slot K1 + e / 8
@@ -174,7 +184,7 @@ __global__ void __launch_bounds__(kNT) build_csp_kernel(CspTables tb, const floa
     tb.bidx[(size_t)r * kBK * kNT + (i / (NPAIR * kBL)) * kNT + i % (NPAIR * kBL)] = 0xFFFFu;
   __syncthreads();
   for (int k = tid; k < NEUR; k += kNT) {
-    const int c = k / 2, rsel = k % 2, w = c / 4;
+    const int c = k / 2, rsel = k % 2, w = warp_of(c / 4), ps = w * 4 + c % 4;
     const int row = order[rsel ? NEUR - 1 - c : c];
     const int base = rsel ? k1w[w] : 0, lim = rsel ? k2w[w] : k1w[w];
     if (cnt[row] > kBL * lim) atomicOr(tb.overflow, 1);
@@ -200,7 +210,7 @@ __global__ void __launch_bounds__(kNT) build_csp_kernel(CspTables tb, const floa
         if (cls[bb] && e < kBL * lim) {
           const int j = __ffsll((long long)cls[bb]) - 1;
           cls[bb] &= cls[bb] - 1;
-          tb.bidx[(size_t)r * kBK * kNT + (base + e / kBL) * kNT + c * kBL + e % kBL] = (uint16_t)(8 * j + bb);
+          tb.bidx[(size_t)r * kBK * kNT + (base + e / kBL) * kNT + ps * kBL + e % kBL] = (uint16_t)(8 * j + bb);
           ++e;
           more = true;
         }
@@ -212,7 +222,7 @@ __global__ void __launch_bounds__(kNT) build_csp_kernel(CspTables tb, const floa
 // ---- forward --------------------------------------------------------------------
 // scratch: vstate [2][HP][BP] neuron-major (BP = planned sample capacity)
 template <int NEUR>
-__global__ void __launch_bounds__(kNT, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb, int BP) {
+__global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb, int BP) {
   constexpr int HP = NEUR * kCL;
   extern __shared__ __align__(16) float smem[];
   float4* cst = reinterpret_cast<float4*>(smem);                          // [kFCap]
@@ -232,10 +242,10 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb
   const long long SV = (long long)HP * BP;
   const bool bad = *tb.overflow != 0;
 
-  for (int i = tid; i <= NEUR; i += kNT) coff[i] = tb.fcoff[r * (NEUR + 1) + i];
+  for (int i = tid; i <= NEUR; i += kNTF) coff[i] = tb.fcoff[r * (NEUR + 1) + i];
   __syncthreads();
   // constants of the own columns' synapses (sigma/2, -sigma*mu/2, w_pos/2, w_erev/2)
-  for (int c = warp; c < NEUR; c += kNT / 32) {
+  for (int c = warp; c < NEUR; c += kNTF / 32) {
     const int q = nb + c;
     float se = 0.f, sp = 0.f;
     for (int e = coff[c] + lane; e < coff[c + 1]; e += 32) {
@@ -258,7 +268,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb
     }
   }
   // initial states of the own columns
-  for (int i = tid; i < NEUR * nvalid; i += kNT) {
+  for (int i = tid; i < NEUR * nvalid; i += kNTF) {
     const int c = i / nvalid, s = i % nvalid, q = nb + c;
     vstate[(long long)q * BP + b0 + s] = (a.h0 && q < H) ? a.h0[(long long)(b0 + s) * H + q] : 0.f;
   }
@@ -273,23 +283,28 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb
       float* vn = vstate + (cur ^ 1) * SV;
       for (int g = 0; g < nsg; ++g) {
         const int sb = b0 + g * kFS;  // first sample of the slice (reads past B are never used)
-        for (int i = tid; i < HP * (kFS / 4); i += kNT) {
+        for (int i = tid; i < HP * (kFS / 4); i += kNTF) {
           const int p = i / (kFS / 4), k4 = i % (kFS / 4);
           cp_async16(vs + p * kFS + 4 * k4, vc + (long long)p * BP + sb + 4 * k4);
         }
         cp_async_commit();
         cp_async_wait_all();
         __syncthreads();
-        const int s = g * kFS + lane;  // this lane's sample in the group
-        for (int c = warp; c < NEUR; c += kNT / 32) {
+        // a slice of <= 16 (<= 8) samples splits each column's list over 2 (4) lane
+        // parts, so the lanes stay busy; the parts' sums are combined by shuffles
+        const int cnt = min(kFS, nvalid - g * kFS);
+        const int F = cnt <= 8 ? 4 : (cnt <= 16 ? 2 : 1), SPL = kFS / F;
+        const int part = lane / SPL, sl = lane % SPL;
+        const int s = g * kFS + sl;  // this lane's sample in the group
+        for (int c = warp; c < NEUR; c += kNTF / 32) {
           const int q = nb + c;
           float an0 = 0.f, an1 = 0.f, ad0 = 0.f, ad1 = 0.f;
-          int e = coff[c];
+          int e = coff[c] + part;
           const int e1 = coff[c + 1];
-          for (; e + 4 <= e1; e += 4) {
-            const float4 k0 = cst[e], k1 = cst[e + 1], k2 = cst[e + 2], k3 = cst[e + 3];
-            const float v0 = vs[ent[e] * kFS + lane], v1 = vs[ent[e + 1] * kFS + lane];
-            const float v2 = vs[ent[e + 2] * kFS + lane], v3 = vs[ent[e + 3] * kFS + lane];
+          for (; e + 3 * F < e1; e += 4 * F) {
+            const float4 k0 = cst[e], k1 = cst[e + F], k2 = cst[e + 2 * F], k3 = cst[e + 3 * F];
+            const float v0 = vs[ent[e] * kFS + sl], v1 = vs[ent[e + F] * kFS + sl];
+            const float v2 = vs[ent[e + 2 * F] * kFS + sl], v3 = vs[ent[e + 3 * F] * kFS + sl];
             const float t0 = tanh_approx(fmaf(k0.x, v0, k0.y)), t1 = tanh_approx(fmaf(k1.x, v1, k1.y));
             const float t2 = tanh_approx(fmaf(k2.x, v2, k2.y)), t3 = tanh_approx(fmaf(k3.x, v3, k3.y));
             an0 = fmaf(k0.w, t0, an0);
@@ -301,18 +316,23 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb
             an1 = fmaf(k3.w, t3, an1);
             ad1 = fmaf(k3.z, t3, ad1);
           }
-          for (; e < e1; ++e) {
+          for (; e < e1; e += F) {
             const float4 k0 = cst[e];
-            const float t0 = tanh_approx(fmaf(k0.x, vs[ent[e] * kFS + lane], k0.y));
+            const float t0 = tanh_approx(fmaf(k0.x, vs[ent[e] * kFS + sl], k0.y));
             an0 = fmaf(k0.w, t0, an0);
             ad0 = fmaf(k0.z, t0, ad0);
           }
-          if (s < nvalid && q < H) {
+          float an = an0 + an1, ad = ad0 + ad1;
+          for (int off = SPL; off < kFS; off *= 2) {
+            an += __shfl_xor_sync(0xffffffffu, an, off);
+            ad += __shfl_xor_sync(0xffffffffu, ad, off);
+          }
+          if (part == 0 && s < nvalid && q < H) {
             const long long bs = b0 + s, row = bs * T + t;
             const float4 nq = a.nrn[q];
-            const float v = vs[q * kFS + lane];
-            const float num = (nq.x * v + nq.w) + ((cw[c] + (an0 + an1)) + a.sn[row * H + q]);
-            const float rr = rcp_approx((nq.x + nq.y) + ((cw[NEUR + c] + (ad0 + ad1)) + a.sd[row * H + q]) + a.eps);
+            const float v = vs[q * kFS + sl];
+            const float num = (nq.x * v + nq.w) + ((cw[c] + an) + a.sn[row * H + q]);
+            const float rr = rcp_approx((nq.x + nq.y) + ((cw[NEUR + c] + ad) + a.sd[row * H + q]) + a.eps);
             const float vnew = bad ? __int_as_float(0x7fc00000) : num * rr;
             vn[(long long)q * BP + bs] = vnew;
             if (a.V) {
@@ -329,7 +349,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_fwd_csp(RecFwdArgs a, CspTables tb
     }
   }
   const float* vc = vstate + cur * SV;
-  for (int i = tid; i < NEUR * nvalid; i += kNT) {
+  for (int i = tid; i < NEUR * nvalid; i += kNTF) {
     const int c = i / nvalid, s = i % nvalid, q = nb + c;
     if (q >= H) continue;
     const long long bs = b0 + s;
@@ -661,13 +681,13 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
 }
 
 template <typename Kern, typename Args>
-cudaError_t launch_c8(Kern kernel, const Args& a, const CspTables& tb, int BP, int grid, size_t smem,
+cudaError_t launch_c8(Kern kernel, const Args& a, const CspTables& tb, int BP, int grid, int threads, size_t smem,
                       cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kNT);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -702,7 +722,8 @@ void plan_csparse(RecPlan& p, int B, int num_clusters) {
   p.wide = true;
   p.ns_fwd = p.ns_bwd = ns;
   p.grid_fwd = p.grid_bwd = ((B + ns - 1) / ns) * kCL;
-  p.threads_fwd = p.threads_bwd = kNT;
+  p.threads_fwd = kNTF;
+  p.threads_bwd = kNT;
   p.slots_bwd = p.grid_bwd / kCL;
   p.smem_fwd = (size_t)kFCap * 16 + (size_t)HP * kFS * 4 + (size_t)kFCap * 2 + (NEUR + 1) * 4 + 2 * NEUR * 4;
   p.smem_bwd = (size_t)kBK * kNT * 16 + (size_t)2 * HP * 4 * kCS4 * 4 + (size_t)2 * 6 * NEUR * kCS * 4 +
@@ -726,14 +747,14 @@ cudaError_t launch_build_csp(const PackArgs& pa, void* tables, cudaStream_t st) 
 
 cudaError_t launch_csp_fwd(const RecFwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st) {
   const CspTables tb = csp_view(const_cast<void*>(tables), p.HP);
-  return p.HP == 512 ? launch_c8(rec_fwd_csp<64>, a, tb, csp_bp(p), p.grid_fwd, p.smem_fwd, st)
-                     : launch_c8(rec_fwd_csp<32>, a, tb, csp_bp(p), p.grid_fwd, p.smem_fwd, st);
+  return p.HP == 512 ? launch_c8(rec_fwd_csp<64>, a, tb, csp_bp(p), p.grid_fwd, kNTF, p.smem_fwd, st)
+                     : launch_c8(rec_fwd_csp<32>, a, tb, csp_bp(p), p.grid_fwd, kNTF, p.smem_fwd, st);
 }
 
 cudaError_t launch_csp_bwd(const RecBwdArgs& a, const RecPlan& p, const void* tables, cudaStream_t st) {
   const CspTables tb = csp_view(const_cast<void*>(tables), p.HP);
-  return p.HP == 512 ? launch_c8(rec_bwd_csp<64>, a, tb, csp_bp(p), p.grid_bwd, p.smem_bwd, st)
-                     : launch_c8(rec_bwd_csp<32>, a, tb, csp_bp(p), p.grid_bwd, p.smem_bwd, st);
+  return p.HP == 512 ? launch_c8(rec_bwd_csp<64>, a, tb, csp_bp(p), p.grid_bwd, kNT, p.smem_bwd, st)
+                     : launch_c8(rec_bwd_csp<32>, a, tb, csp_bp(p), p.grid_bwd, kNT, p.smem_bwd, st);
 }
 
 }  // namespace ltc
