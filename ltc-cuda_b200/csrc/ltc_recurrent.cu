@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
   extern __shared__ __align__(16) float smem[];
   const int ns = a.ns;
   float* vbuf = smem;                // [2][ns][LDV]
-  float* snb = vbuf + 2 * ns * LDV;  // [ns][LDV]
-  float* sdb = snb + ns * LDV;       // [ns][LDV]
+  float* snb2 = vbuf + 2 * ns * LDV;  // [2][ns][LDV]: step t in slot t & 1
+  float* sdb2 = snb2 + 2 * ns * LDV;  // [2][ns][LDV]
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int nb = group_rank<CL>() * G::NEUR;  // first neuron of this CTA
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
     }
   }
   uint32_t xphase = 0;  // parity bit per slot
-  for (int i = tid; i < 4 * ns * LDV; i += NT) smem[i] = 0.f;
+  for (int i = tid; i < 6 * ns * LDV; i += NT) smem[i] = 0.f;
   __syncthreads();
   if (a.h0) {
     for (int i = tid; i < nvalid * H; i += NT) {
@@ -172,17 +172,27 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
       vbuf[s * LDV + h] = a.h0[(long long)(b0 + s) * H + h];
     }
   }
-  group_sync<CL>();  // every CTA of the group initialised before any remote store
-  int cur = 0;
-  for (int t = 0; t < T; ++t) {
-    __syncthreads();
+  // the sensory sums of step t + 1 are copied in (cp.async) while step t unfolds
+  auto stage_sens = [&](int t) {
+    float* dn = snb2 + (t & 1) * ns * LDV;
+    float* dd = sdb2 + (t & 1) * ns * LDV;
     for (int i = tid; i < nvalid * H; i += NT) {
       const int s = i / H, h = i % H;
       const long long row = (long long)(b0 + s) * T + t;
-      snb[s * LDV + h] = a.sn[row * H + h];
-      sdb[s * LDV + h] = a.sd[row * H + h];
+      cp_async4(dn + s * LDV + h, a.sn + row * H + h);
+      cp_async4(dd + s * LDV + h, a.sd + row * H + h);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  stage_sens(0);
+  cp_async_wait_all();
+  group_sync<CL>();  // every CTA of the group initialised before any remote store
+  int cur = 0;
+  for (int t = 0; t < T; ++t) {
+    __syncthreads();  // step t's sums visible; slot (t + 1) & 1 no longer read
+    if (t + 1 < T) stage_sens(t + 1);
+    const float* __restrict__ snb = snb2 + (t & 1) * ns * LDV;
+    const float* __restrict__ sdb = sdb2 + (t & 1) * ns * LDV;
     for (int u = 0; u < U; ++u) {
       const long long n = (long long)t * U + u;
       const float* __restrict__ vc = vbuf + cur * ns * LDV;
@@ -251,6 +261,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
       }
       cur ^= 1;
     }
+    cp_async_wait_all();
   }
   if constexpr (CL > 1) {  // the last unfold's v from every CTA of the group
     for (int blk = 0; blk < nblk; ++blk)
@@ -289,8 +300,9 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   float* RS = VS + 3 * SL;   // [2]
   float* DIR = RS + 2 * SL;
   float* GSN = DIR + SL;
-  float* GSD = GSN + SL;     // 13 slabs, then [5][HP][TPC] for the final per-neuron sums
-  float* red = GSD + SL;
+  float* GSD = GSN + SL;
+  float* GO = GSD + SL;      // [2]: 15 slabs, then [5][HP][TPC] for the final per-neuron sums
+  float* red = GO + 2 * SL;
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int nb = group_rank<CL>() * G::NEUR;  // first row of this CTA
@@ -344,7 +356,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     }
   }
   uint32_t xphase = 0;  // parity bit per slot
-  for (int i = tid; i < 13 * SL; i += NT) smem[i] = 0.f;
+  for (int i = tid; i < 15 * SL; i += NT) smem[i] = 0.f;
   __syncthreads();
 
   // stage saved slices: V[m] -> VS[m%3], R[m] -> RS[m%2]
@@ -358,6 +370,19 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     const float* src = a.R + ((long long)m * B + b0) * H;
     for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
   };
+  // dL/dout of step tt (strided) -> GO[tt & 1], copied in while later unfolds run;
+  // a gradient broadcast over samples and steps (stride 0, e.g. a sum loss) is
+  // read in place: it is H values that stay in cache
+  const bool go_bcast = a.go_sb == 0 && a.go_st == 0;
+  auto stage_go = [&](int tt) {
+    if (go_bcast) return;
+    float* dst = GO + (tt & 1) * SL;
+    for (int i = tid; i < nvalid * H; i += NT) {
+      const int s = i / H, h = i % H;
+      cp_async4(dst + s * LDV + h, a.gout + (long long)(b0 + s) * a.go_sb + (long long)tt * a.go_st +
+                                       (long long)h * a.go_sh);
+    }
+  };
   stage_v(NTU);
   stage_v(NTU - 1);
   stage_r(NTU - 1);
@@ -365,6 +390,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     stage_v(NTU - 2);
     stage_r(NTU - 2);
   }
+  if (T >= 2) stage_go(T - 2);
   cp_async_commit();
   cp_async_wait_all();
   group_sync<CL>();  // every CTA of the group initialised before any remote store
@@ -435,6 +461,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       stage_v(n - 2);
       stage_r(n - 2);
     }
+    if (k == 0 && t >= 2) stage_go(t - 2);  // read at step t - 1's last unfold, >= 1 unfold later
     cp_async_commit();
 
     const int c2 = n % 2, c2m = c2 ^ 1;          // slots of unfold n and n-1 (mod 2)
@@ -503,7 +530,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
             a.gh0[bs * H + p] = gval;
             done = true;
           } else {
-            gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
+            gval += go_bcast ? a.gout[(long long)p * a.go_sh] : GO[((t - 1) & 1) * SL + idx];
           }
         }
         if (!done) prep(rsm, vsm, vsn, an_m, ad_m, s, gval, k == 0);
@@ -604,7 +631,7 @@ bool grouping_ok(int B, int ns, int grid, size_t smem, size_t need_floats) {
 
 template <int HP>
 cudaError_t launch_fast_fwd(const RecFwdArgs& a, const RecPlan& pl, cudaStream_t st) {
-  if (!grouping_ok<HP>(a.B, a.ns, pl.grid_fwd, pl.smem_fwd, (size_t)4 * a.ns * (HP + 4)))
+  if (!grouping_ok<HP>(a.B, a.ns, pl.grid_fwd, pl.smem_fwd, (size_t)6 * a.ns * (HP + 4)))
     return cudaErrorInvalidValue;
   return launch_grouped<cluster_of<HP>()>(rec_fwd_fast<HP>, a, pl.grid_fwd,
                                           Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>::NT, pl.smem_fwd, st);
@@ -613,7 +640,7 @@ cudaError_t launch_fast_fwd(const RecFwdArgs& a, const RecPlan& pl, cudaStream_t
 template <int HP>
 cudaError_t launch_fast_bwd(const RecBwdArgs& a, const RecPlan& pl, cudaStream_t st) {
   if (!grouping_ok<HP>(a.B, a.ns, pl.grid_bwd, pl.smem_bwd,
-                       (size_t)13 * a.ns * (HP + 4) + 5 * HP * (HP / 8)))
+                       (size_t)15 * a.ns * (HP + 4) + 5 * HP * (HP / 8)))
     return cudaErrorInvalidValue;
   return launch_grouped<cluster_of<HP>()>(rec_bwd_fast<HP>, a, pl.grid_bwd,
                                           Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>::NT, pl.smem_bwd, st);
@@ -700,9 +727,9 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide, bool skip_zero
   const int groups = CL > 1 ? resident_clusters(CL, num_sms) : num_sms;
   const int blocks = (B + kSB - 1) / kSB;
   // each kernel: an equal share of sample blocks per resident sample group
-  // shared-memory bound of the backward kernel (13 per-sample slabs + the reduction area)
+  // shared-memory bound of the backward kernel (15 per-sample slabs + the reduction area)
   const size_t smem_cap = 227 * 1024 - 1024;
-  const int max_per = (int)((smem_cap - 5 * HP * (HP / 8) * sizeof(float)) / (13 * LDV * sizeof(float) * kSB));
+  const int max_per = (int)((smem_cap - 5 * HP * (HP / 8) * sizeof(float)) / (15 * LDV * sizeof(float) * kSB));
   // blocks per group: as many waves of resident groups as the per-group cap
   // forces, and the blocks spread evenly over them (a ragged last wave costs a
   // full one)
@@ -724,8 +751,8 @@ RecPlan plan_recurrent(int B, int H, int num_sms, int force_wide, bool skip_zero
   p.threads_fwd = HP * HP / 8 / CL / (h64 ? LTC_FWD_RPT : 1);
   p.threads_bwd = HP * HP / 8 / CL / (HP >= 128 ? LTC_BWD_RPT128 : h64 ? LTC_BWD_RPT : 1);
   p.slots_bwd = p.grid_bwd / CL;
-  p.smem_fwd = (size_t)4 * p.ns_fwd * LDV * sizeof(float);
-  p.smem_bwd = ((size_t)13 * p.ns_bwd * LDV + 5 * HP * (HP / 8)) * sizeof(float);
+  p.smem_fwd = (size_t)6 * p.ns_fwd * LDV * sizeof(float);
+  p.smem_bwd = ((size_t)15 * p.ns_bwd * LDV + 5 * HP * (HP / 8)) * sizeof(float);
   p.tanh_space = true;
   return p;
 }

@@ -308,8 +308,8 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
   const int ns = a.ns;
   const int S = 4 * neuron_stride4(ns);
   float* vbuf = smem;                 // [2][HP][S]
-  float* snb = vbuf + 2 * HP * S;     // [ns][LDV]
-  float* sdb = snb + ns * LDV;        // [ns][LDV]
+  float* snb2 = vbuf + 2 * HP * S;    // [2][ns][LDV]: step t in slot t & 1
+  float* sdb2 = snb2 + 2 * ns * LDV;  // [2][ns][LDV]
 
   const int tid = threadIdx.x, lane = tid & 31, c = tid / TPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
   const bool qvalid = q < H;
   const bool writer = LR::writer(lane);
 
-  for (int i = tid; i < 2 * HP * S + 2 * ns * LDV; i += NT) smem[i] = 0.f;
+  for (int i = tid; i < 2 * HP * S + 4 * ns * LDV; i += NT) smem[i] = 0.f;
   __syncthreads();
   if (a.h0) {
     for (int i = tid; i < nvalid * H; i += NT) {
@@ -355,16 +355,26 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
       vbuf[h * S + s] = a.h0[(long long)(b0 + s) * H + h];
     }
   }
-  int cur = 0;
-  for (int t = 0; t < T; ++t) {
-    __syncthreads();
+  // the sensory sums of step t + 1 are copied in (cp.async) while step t unfolds
+  auto stage_sens = [&](int t) {
+    float* dn = snb2 + (t & 1) * ns * LDV;
+    float* dd = sdb2 + (t & 1) * ns * LDV;
     for (int i = tid; i < nvalid * H; i += NT) {
       const int s = i / H, h = i % H;
       const long long row = (long long)(b0 + s) * T + t;
-      snb[s * LDV + h] = a.sn[row * H + h];
-      sdb[s * LDV + h] = a.sd[row * H + h];
+      cp_async4(dn + s * LDV + h, a.sn + row * H + h);
+      cp_async4(dd + s * LDV + h, a.sd + row * H + h);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  stage_sens(0);
+  cp_async_wait_all();
+  int cur = 0;
+  for (int t = 0; t < T; ++t) {
+    __syncthreads();  // step t's sums visible; slot (t + 1) & 1 no longer read
+    if (t + 1 < T) stage_sens(t + 1);
+    const float* __restrict__ snb = snb2 + (t & 1) * ns * LDV;
+    const float* __restrict__ sdb = sdb2 + (t & 1) * ns * LDV;
     for (int u = 0; u < U; ++u) {
       const long long n = (long long)t * U + u;
       const float* __restrict__ vc = vbuf + cur * HP * S;
@@ -396,6 +406,7 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
       __syncthreads();
       cur ^= 1;
     }
+    cp_async_wait_all();
   }
   const float* vc = vbuf + cur * HP * S;
   for (int i = tid; i < nvalid * H; i += NT) {
@@ -476,7 +487,8 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
   float* DIR = RS + 2 * SL;
   float* GSN = DIR + SL;
   float* GSD = GSN + SL;
-  float* red = GSD + SL;        // [5][HP][kTPC]
+  float* GO = GSD + SL;         // [2][SL]
+  float* red = GO + 2 * SL;     // [5][HP][kTPC]
 
   const int tid = threadIdx.x, lane = tid & 31, c = tid / kTPC, g = tid % kTPC;
   const int H = a.H, B = a.B, T = a.T, U = a.U;
@@ -515,7 +527,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
   const bool writer = LR::writer(lane);
   float gcm = bad, ggl = bad, gvl = bad, san = bad, sad = bad;
 
-  for (int i = tid; i < 4 * SA + 8 * SL; i += NT) smem[i] = 0.f;
+  for (int i = tid; i < 4 * SA + 10 * SL; i += NT) smem[i] = 0.f;
   __syncthreads();
 
   auto stage_v = [&](int m) {
@@ -528,6 +540,19 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
     const float* src = a.R + ((long long)m * B + b0) * H;
     for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
   };
+  // dL/dout of step tt (strided) -> GO[tt & 1], copied in while later unfolds run;
+  // a gradient broadcast over samples and steps (stride 0, e.g. a sum loss) is
+  // read in place: it is H values that stay in cache
+  const bool go_bcast = a.go_sb == 0 && a.go_st == 0;
+  auto stage_go = [&](int tt) {
+    if (go_bcast) return;
+    float* dst = GO + (tt & 1) * SL;
+    for (int i = tid; i < nvalid * H; i += NT) {
+      const int s = i / H, h = i % H;
+      cp_async4(dst + s * LDV + h, a.gout + (long long)(b0 + s) * a.go_sb + (long long)tt * a.go_st +
+                                       (long long)h * a.go_sh);
+    }
+  };
   stage_v(NTU);
   stage_v(NTU - 1);
   stage_r(NTU - 1);
@@ -535,6 +560,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
     stage_v(NTU - 2);
     stage_r(NTU - 2);
   }
+  if (T >= 2) stage_go(T - 2);
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
@@ -582,6 +608,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
       stage_v(n - 2);
       stage_r(n - 2);
     }
+    if (k == 0 && t >= 2) stage_go(t - 2);  // read at step t - 1's last unfold, >= 1 unfold later
     cp_async_commit();
     const int c2 = n % 2, c2m = c2 ^ 1;
     const int c3 = n % 3, c3m = (n + 2) % 3;
@@ -615,7 +642,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
             a.gh0[bs * H + p] = gval;
             done = true;
           } else {
-            gval += a.gout[bs * a.go_sb + (long long)(t - 1) * a.go_st + (long long)p * a.go_sh];
+            gval += go_bcast ? a.gout[(long long)p * a.go_sh] : GO[((t - 1) & 1) * SL + idx];
           }
         }
         if (!done) prep(rsm, vsm, vsn, an_m, ad_m, s, gval, k == 0);
@@ -699,10 +726,10 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
   const int LDV = HP + 4;
   const int blocks = (B + kSB - 1) / kSB;
   const size_t smem_cap = 227 * 1024 - 1024;
-  // backward: 4 neuron-major adjoint slabs + 8 [ns][LDV] slabs + the reduction area
+  // backward: 4 neuron-major adjoint slabs + 10 [ns][LDV] slabs + the reduction area
   auto bwd_bytes = [&](int ns) {
     const int S = 4 * neuron_stride4(ns);
-    return ((size_t)4 * HP * S + 8 * (size_t)ns * LDV + 5 * HP * side_tpc(0)) * sizeof(float);
+    return ((size_t)4 * HP * S + 10 * (size_t)ns * LDV + 5 * HP * side_tpc(0)) * sizeof(float);
   };
   int cap = 1;
   while (bwd_bytes((cap + 1) * kSB) <= smem_cap) ++cap;
@@ -720,7 +747,7 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
   p.threads_fwd = side_nt(HP, 1);
   p.threads_bwd = side_nt(HP, 0);
   p.slots_bwd = p.grid_bwd;
-  p.smem_fwd = ((size_t)2 * HP * S + 2 * (size_t)ns * LDV) * sizeof(float);
+  p.smem_fwd = ((size_t)2 * HP * S + 4 * (size_t)ns * LDV) * sizeof(float);
   p.smem_bwd = bwd_bytes(ns);
   p.tanh_space = true;
 }
