@@ -79,7 +79,10 @@ def measured_peaks():
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of this rank's GPU while the timed region runs."""
+    """nvidia-smi samples (50 ms) of this rank's GPU while the timed region runs.
+
+    ``start`` returns once the first sample is in, so that nvidia-smi's own start-up
+    (which touches every GPU of the machine) is not inside the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -94,13 +97,17 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        t0 = time.time()
+        while not self.rows and self.proc.poll() is None and time.time() - t0 < 10:
+            time.sleep(0.01)
+        self.rows.clear()
 
     def _read(self):
         for line in self.proc.stdout:

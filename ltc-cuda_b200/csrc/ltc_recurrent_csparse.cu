@@ -283,56 +283,76 @@ __global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables t
       float* vn = vstate + (cur ^ 1) * SV;
       for (int g = 0; g < nsg; ++g) {
         const int sb = b0 + g * kFS;  // first sample of the slice (reads past B are never used)
-        for (int i = tid; i < HP * (kFS / 4); i += kNTF) {
-          const int p = i / (kFS / 4), k4 = i % (kFS / 4);
+        const int cnt = min(kFS, nvalid - g * kFS);
+        const int n4 = (cnt + 3) / 4;  // float4 per neuron that hold the slice's samples
+        for (int i = tid; i < HP * n4; i += kNTF) {
+          const int p = i / n4, k4 = i % n4;
           cp_async16(vs + p * kFS + 4 * k4, vc + (long long)p * BP + sb + 4 * k4);
         }
         cp_async_commit();
         cp_async_wait_all();
         __syncthreads();
-        // a slice of <= 16 (<= 8) samples splits each column's list over 2 (4) lane
-        // parts, so the lanes stay busy; the parts' sums are combined by shuffles
-        const int cnt = min(kFS, nvalid - g * kFS);
-        const int F = cnt <= 8 ? 4 : (cnt <= 16 ? 2 : 1), SPL = kFS / F;
-        const int part = lane / SPL, sl = lane % SPL;
-        const int s = g * kFS + sl;  // this lane's sample in the group
+        // Lane = (sample quad sq, list part): each lane runs 4 samples per synapse
+        // entry (one float4 gather, the entry's constants loaded once), the column's
+        // list is split over F = 32 / SQ parts (SQ = quads in the slice, a power of
+        // two, so a short slice still fills the warp), and a transposed shuffle
+        // reduction over the parts leaves one sample of the column per owner lane.
+        const int SQ = cnt <= 4 ? 1 : cnt <= 8 ? 2 : cnt <= 16 ? 4 : 8, F = 32 / SQ;
+        const int sq = lane % SQ, part = lane / SQ;
+        const bool hA = part & (F / 2), hB = part & (F / 4);
+        const bool lead = (part & (F / 4 - 1)) == 0;
+        const int s = g * kFS + 4 * sq + 2 * hA + hB;  // the sample this lane owns if lead
         for (int c = warp; c < NEUR; c += kNTF / 32) {
           const int q = nb + c;
-          float an0 = 0.f, an1 = 0.f, ad0 = 0.f, ad1 = 0.f;
+          // the tail's global reads are issued before the synapse pass hides their latency
+          const bool owner = lead && s < nvalid && q < H;
+          const long long row = (long long)(b0 + s) * T + t;
+          float snv = 0.f, sdv = 0.f;
+          float4 nq = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (owner) {
+            snv = a.sn[row * H + q];
+            sdv = a.sd[row * H + q];
+            nq = a.nrn[q];
+          }
+          float an[4] = {0.f, 0.f, 0.f, 0.f}, ad[4] = {0.f, 0.f, 0.f, 0.f};
+          auto visit = [&](int e) {
+            const float4 k = cst[e];
+            const float4 v = *reinterpret_cast<const float4*>(vs + ent[e] * kFS + 4 * sq);
+            const float th[4] = {tanh_approx(fmaf(k.x, v.x, k.y)), tanh_approx(fmaf(k.x, v.y, k.y)),
+                                 tanh_approx(fmaf(k.x, v.z, k.y)), tanh_approx(fmaf(k.x, v.w, k.y))};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              an[i] = fmaf(k.w, th[i], an[i]);
+              ad[i] = fmaf(k.z, th[i], ad[i]);
+            }
+          };
           int e = coff[c] + part;
           const int e1 = coff[c + 1];
-          for (; e + 3 * F < e1; e += 4 * F) {
-            const float4 k0 = cst[e], k1 = cst[e + F], k2 = cst[e + 2 * F], k3 = cst[e + 3 * F];
-            const float v0 = vs[ent[e] * kFS + sl], v1 = vs[ent[e + F] * kFS + sl];
-            const float v2 = vs[ent[e + 2 * F] * kFS + sl], v3 = vs[ent[e + 3 * F] * kFS + sl];
-            const float t0 = tanh_approx(fmaf(k0.x, v0, k0.y)), t1 = tanh_approx(fmaf(k1.x, v1, k1.y));
-            const float t2 = tanh_approx(fmaf(k2.x, v2, k2.y)), t3 = tanh_approx(fmaf(k3.x, v3, k3.y));
-            an0 = fmaf(k0.w, t0, an0);
-            ad0 = fmaf(k0.z, t0, ad0);
-            an1 = fmaf(k1.w, t1, an1);
-            ad1 = fmaf(k1.z, t1, ad1);
-            an0 = fmaf(k2.w, t2, an0);
-            ad0 = fmaf(k2.z, t2, ad0);
-            an1 = fmaf(k3.w, t3, an1);
-            ad1 = fmaf(k3.z, t3, ad1);
+          for (; e + F < e1; e += 2 * F) {
+            visit(e);
+            visit(e + F);
           }
-          for (; e < e1; e += F) {
-            const float4 k0 = cst[e];
-            const float t0 = tanh_approx(fmaf(k0.x, vs[ent[e] * kFS + sl], k0.y));
-            an0 = fmaf(k0.w, t0, an0);
-            ad0 = fmaf(k0.z, t0, ad0);
+          if (e < e1) visit(e);
+          // parts F/2 apart: keep samples (2, 3) or (0, 1), send the other pair
+          float a2[2], d2[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const float sa = hA ? an[i] : an[2 + i], sd_ = hA ? ad[i] : ad[2 + i];
+            a2[i] = (hA ? an[2 + i] : an[i]) + __shfl_xor_sync(0xffffffffu, sa, 16);
+            d2[i] = (hA ? ad[2 + i] : ad[i]) + __shfl_xor_sync(0xffffffffu, sd_, 16);
           }
-          float an = an0 + an1, ad = ad0 + ad1;
-          for (int off = SPL; off < kFS; off *= 2) {
-            an += __shfl_xor_sync(0xffffffffu, an, off);
-            ad += __shfl_xor_sync(0xffffffffu, ad, off);
+          // parts F/4 apart: keep one sample of the pair
+          float an1 = (hB ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, hB ? a2[0] : a2[1], 8);
+          float ad1 = (hB ? d2[1] : d2[0]) + __shfl_xor_sync(0xffffffffu, hB ? d2[0] : d2[1], 8);
+          for (int off = SQ; off < 8; off *= 2) {  // the remaining part bits: plain sums
+            an1 += __shfl_xor_sync(0xffffffffu, an1, off);
+            ad1 += __shfl_xor_sync(0xffffffffu, ad1, off);
           }
-          if (part == 0 && s < nvalid && q < H) {
-            const long long bs = b0 + s, row = bs * T + t;
-            const float4 nq = a.nrn[q];
-            const float v = vs[q * kFS + sl];
-            const float num = (nq.x * v + nq.w) + ((cw[c] + an) + a.sn[row * H + q]);
-            const float rr = rcp_approx((nq.x + nq.y) + ((cw[NEUR + c] + ad) + a.sd[row * H + q]) + a.eps);
+          if (owner) {
+            const long long bs = b0 + s;
+            const float v = vs[q * kFS + (s - g * kFS)];
+            const float num = (nq.x * v + nq.w) + ((cw[c] + an1) + snv);
+            const float rr = rcp_approx((nq.x + nq.y) + ((cw[NEUR + c] + ad1) + sdv) + a.eps);
             const float vnew = bad ? __int_as_float(0x7fc00000) : num * rr;
             vn[(long long)q * BP + bs] = vnew;
             if (a.V) {
