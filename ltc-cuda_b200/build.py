@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libltc_sm100.so")
 SOURCES = ["ltc_capi.cu", "ltc_prep.cu", "ltc_sensory.cu", "ltc_recurrent.cu", "ltc_recurrent_wide.cu",
            "ltc_noalloc.cu", "ltc_recurrent_stream.cu", "ltc_recurrent_sparse.cu", "ltc_recurrent_csparse.cu",
-           "ltc_preamble.cu"]
+           "ltc_preamble.cu", "ltc_sensory_sparse.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -126,6 +126,7 @@ struct Layout {
   long long rows;
   size_t saved_floats_v, saved_floats_r;
   bool lean;  // LTC_FLAG_LEAN_SAVE: saved = step-boundary states; the backward recomputes segments
+  bool skip_sens;  // LTC_FLAG_SKIP_ZERO_SYNAPSES: the sensory forward visits only sw != 0
   int tc;     // lean segment length in steps
 };
 
@@ -149,6 +150,8 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
   L->rp = plan_recurrent(d->B, d->H, di->sms, d->flags & LTC_FLAG_FORCE_WIDE,
                          (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) != 0);
   L->rows = (long long)d->B * d->T;
+  L->skip_sens = (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) && !(d->flags & LTC_FLAG_FORCE_WIDE) &&
+                 sens_sparse_fits(d->D);
   L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
   const size_t tu = (size_t)d->T * d->ode_unfolds;
   L->lean = (d->flags & LTC_FLAG_LEAN_SAVE) != 0;
@@ -177,7 +180,8 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
 struct FwdBuffers {
   float4 *pack, *spack, *nrn;
   float *sn, *sd, *scratch;
-  void* tables;  // sparse path only
+  void* tables;   // sparse path only
+  void* stables;  // sensory lists (skip_sens only)
 };
 size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
   Carver c(ws);
@@ -189,6 +193,7 @@ size_t carve_fwd(const LtcDims* d, const Layout& L, void* ws, FwdBuffers* b) {
   b->sd = c.take<float>((size_t)L.rows * d->H);
   b->scratch = L.rp.scratch_fwd ? c.take<float>(L.rp.scratch_fwd) : nullptr;
   b->tables = L.rp.sparse ? c.take<char>(sparse_tables_bytes(HP)) : nullptr;
+  b->stables = L.skip_sens ? c.take<char>(sens_tables_bytes(d->D, HP)) : nullptr;
   return c.off + 256;
 }
 
@@ -197,7 +202,8 @@ struct BwdBuffers {
   float *gsn, *gsd, *rpart, *rpartn, *spart, *dxpart, *scratch;
   // lean backward: one segment's staged inputs, recomputed state and outputs
   float *xc, *snc, *sdc, *gsnc, *gsdc, *Vc, *Rc, *hs, *ghA, *ghB, *fscratch;
-  void* tables;  // sparse path only
+  void* tables;   // sparse path only
+  void* stables;  // sensory lists (lean recompute with skip_sens only)
 };
 size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   Carver c(ws);
@@ -214,6 +220,7 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->dxpart = L.sp.dxpart_floats ? c.take<float>(L.sp.dxpart_floats) : nullptr;
   b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
   b->tables = L.rp.sparse ? c.take<char>(sparse_tables_bytes(HP)) : nullptr;
+  b->stables = L.lean && L.skip_sens ? c.take<char>(sens_tables_bytes(d->D, HP)) : nullptr;
   b->xc = b->snc = b->sdc = b->gsnc = b->gsdc = b->Vc = b->Rc = b->hs = b->ghA = b->ghB = b->fscratch = nullptr;
   if (L.lean) {
     const size_t BH = (size_t)d->B * d->H, tcu = (size_t)L.tc * d->ode_unfolds;
@@ -411,13 +418,18 @@ int ltc_forward(const LtcDims* dims, const LtcParams* params, const float* x, co
     e = launch_build_slots(pa, b.tables, st);
     if (e != cudaSuccess) return cuda_fail(e, "build_slots");
   }
+  if (L.skip_sens) {
+    TimedLaunch tl(LTC_KERNEL_PACK_FWD, st);
+    e = launch_build_sens(pa, b.stables, st);
+    if (e != cudaSuccess) return cuda_fail(e, "build_sens");
+  }
 
   SensFwdArgs sa{};
   sa.spack = b.spack; sa.x = x; sa.sn = b.sn; sa.sd = b.sd; sa.rows = L.rows;
   sa.D = dims->D; sa.H = dims->H; sa.HP = HP;
   {
     TimedLaunch tl(LTC_KERNEL_SENSORY_FWD, st);
-    e = launch_sensory_fwd(sa, di.sms, st);
+    e = L.skip_sens ? launch_sensory_fwd_sparse(sa, b.stables, di.sms, st) : launch_sensory_fwd(sa, di.sms, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sensory_fwd");
 
@@ -484,6 +496,11 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
     TimedLaunch tl(LTC_KERNEL_PACK_BWD, st);
     e = launch_build_slots(pa, b.tables, st);
     if (e != cudaSuccess) return cuda_fail(e, "build_slots");
+  }
+  if (b.stables) {
+    TimedLaunch tl(LTC_KERNEL_PACK_BWD, st);
+    e = launch_build_sens(pa, b.stables, st);
+    if (e != cudaSuccess) return cuda_fail(e, "build_sens");
   }
 
   Carver sc(const_cast<void*>(saved));
@@ -573,7 +590,7 @@ int lean_recurrent_backward(const LtcDims* dims, const Layout& L, const DeviceIn
     sa.D = D; sa.H = H; sa.HP = HP;
     {
       TimedLaunch tl(LTC_KERNEL_SENSORY_FWD, st);
-      e = launch_sensory_fwd(sa, di.sms, st);
+      e = b.stables ? launch_sensory_fwd_sparse(sa, b.stables, di.sms, st) : launch_sensory_fwd(sa, di.sms, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "lean: sensory_fwd");
     RecFwdArgs fa{};

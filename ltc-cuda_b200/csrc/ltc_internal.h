@@ -41,6 +41,12 @@ struct SensFwdArgs {
   int D, H, HP;
 };
 cudaError_t launch_sensory_fwd(const SensFwdArgs& a, int num_sms, cudaStream_t st);
+// masked sensory synapses skipped (ltc_sensory_sparse.cu): per-column lists of the
+// nonzero inputs, built on the device after the pack (sens_tables_bytes of workspace)
+size_t sens_tables_bytes(int D, int HP);
+bool sens_sparse_fits(int D);
+cudaError_t launch_build_sens(const PackArgs& pa, void* tables, cudaStream_t st);
+cudaError_t launch_sensory_fwd_sparse(const SensFwdArgs& a, const void* tables, int num_sms, cudaStream_t st);
 
 // ---- sensory backward ----------------------------------------------------
 struct SensBwdArgs {
