@@ -59,7 +59,10 @@ typedef struct {
  * neuron and at most 8192 enter each block of HP/8 consecutive neurons (HP = 256
  * for H <= 256, else 512).  The library cannot
  * report a violation without a device sync, so a call that exceeds it writes NaN
- * to its outputs and gradients; check the pattern before setting the flag. */
+ * to its outputs and gradients; check the pattern before setting the flag.
+ * The same flag makes the sensory forward visit only the sensory synapses with
+ * sensory_w_pos != 0 (any pattern; D up to 682, larger D keeps the dense pass); that changes no output
+ * beyond summation order and no gradient. */
 #define LTC_FLAG_SKIP_ZERO_SYNAPSES 4
 /* Bits 8..23 of flags, if nonzero, fix the lean segment length in steps
  * (otherwise it is sized for about 512 MiB of per-unfold state). */

@@ -83,7 +83,8 @@ __global__ void __launch_bounds__(256) build_sens_kernel(SensTablesView tv, cons
   }
 }
 
-constexpr int kNT = 512, kQB = 64;  // threads; columns per output pass
+constexpr int kNT = 512, kQB = 32;  // threads; columns per output pass
+constexpr int kLC = 128;            // list entries a warp stages in shared memory at a time
 
 template <int RPL>
 struct RowVec;
@@ -107,10 +108,13 @@ struct RowVec<4> {
 };
 
 __host__ __device__ constexpr size_t sens_sparse_smem(int D, int rpl, int nbuf) {
-  return ((size_t)nbuf * D * 32 * rpl + (size_t)2 * 32 * rpl * (kQB + 1)) * sizeof(float);
+  return ((size_t)nbuf * D * 32 * rpl + (size_t)2 * 32 * rpl * (kQB + 1)) * sizeof(float) +
+         (size_t)(kNT / 32) * kLC * (sizeof(float4) + sizeof(int));
 }
 
-// xs [nbuf][D][TR] (x tile transposed: row r of input d at d * TR + r), os [2][TR][kQB + 1]
+// xs [nbuf][D][TR] (x tile transposed: row r of input d at d * TR + r), os [2][TR][kQB + 1],
+// then per warp kLC list entries (constants, indices): a column's list is brought in
+// with coalesced loads, kLC entries at a time, so the walk waits on no global load
 template <int RPL>
 __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTablesView tv, int nbuf) {
   constexpr int TR = 32 * RPL, LDO = kQB + 1;
@@ -119,6 +123,9 @@ __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTab
   float* xs = smem;
   float* osn = xs + (size_t)nbuf * D * TR;
   float* osd = osn + TR * LDO;
+  float4* lcs = reinterpret_cast<float4*>(osd + TR * LDO) + (threadIdx.x / 32) * kLC;
+  int* lis = reinterpret_cast<int*>(reinterpret_cast<float4*>(osd + TR * LDO) + (kNT / 32) * kLC) +
+             (threadIdx.x / 32) * kLC;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const long long ntiles = (a.rows + TR - 1) / TR;
 
@@ -154,9 +161,9 @@ __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTab
 #pragma unroll
         for (int i = 0; i < RPL; ++i) sn[i] = sd[i] = 0.f;
         auto visit = [&](int k) {
-          const float4 w = lc[k];
+          const float4 w = lcs[k];
           float xv[RPL];
-          RowVec<RPL>::load(xt + li[k] * TR, xv);
+          RowVec<RPL>::load(xt + lis[k] * TR, xv);
 #pragma unroll
           for (int i = 0; i < RPL; ++i) {
             const float th = tanh_approx(fmaf(w.x, xv[i], w.y));
@@ -164,14 +171,27 @@ __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTab
             sd[i] = fmaf(w.z, th, sd[i]);
           }
         };
-        int k = 0;
-        for (; k + 3 < n; k += 4) {
-          visit(k);
-          visit(k + 1);
-          visit(k + 2);
-          visit(k + 3);
+        for (int base = 0; base < n; base += kLC) {
+          const int m = min(kLC, n - base);
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < kLC / 32; ++j) {
+            const int k = j * 32 + lane;
+            if (k < m) {
+              lcs[k] = lc[base + k];
+              lis[k] = li[base + k];
+            }
+          }
+          __syncwarp();
+          int k = 0;
+          for (; k + 3 < m; k += 4) {
+            visit(k);
+            visit(k + 1);
+            visit(k + 2);
+            visit(k + 3);
+          }
+          for (; k < m; ++k) visit(k);
         }
-        for (; k < n; ++k) visit(k);
         const float2 cw = tv.cw[q];
 #pragma unroll
         for (int i = 0; i < RPL; ++i) {  // act = 1/2 + tanh/2: the constant half is the column sum
