@@ -239,3 +239,22 @@ def test_wide_determinism_and_lean():
     assert torch.equal(c[0], a[0])
     for k in FN:
         assert rel_err(c[2][k], a[2][k]) < 1e-5, k
+
+
+@pytest.mark.parametrize("D", [40, 300, 600, 700])
+def test_sensory_lists_vs_oracle(D):
+    """Skipped sensory synapses: empty and full columns, every shared-memory geometry of
+    the sensory list pass (double- and single-buffered tiles of 4 rows per lane, 2 rows
+    per lane) and, at D = 700, the dense fallback."""
+    H = 64
+    p = synth.make_params(D, H, 0.5, 0.3, seed=D)
+    smask = p["sensory_sparsity_mask"].clone()
+    smask[:, 3] = 0.0       # a column with no input
+    smask[:, 5] = 1.0       # a column with every input
+    smask[D // 2, :] = 0.0  # an input feeding nothing
+    p["sensory_sparsity_mask"] = smask
+    g = torch.Generator().manual_seed(D)
+    x = torch.randn(7, 6, D, generator=g)
+    inp = {k: v.detach() for k, v in orc.module_preamble(p, x, 1 / 30, 3).items()}
+    inp["state"] = torch.randn(7, H, generator=g) * 0.3
+    _check(inp, 3, torch.randn(7, 6, H, generator=g), torch.randn(7, H, generator=g), f"D{D}")
