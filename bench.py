@@ -320,10 +320,22 @@ def rec_synapses(model, cfg, rows) -> int:
     return cfg.H * cfg.H
 
 
-def our_parity(cfg, p, dev):
+def our_parity(cfg, p, dev, skip_zero=True):
     """Parity of this build's module on a slice of the timed configuration, checked
     before the timed region against the reference TorchScript path (or, where the
-    reference is not staged, the oracle restatement of it)."""
+    reference is not staged, the oracle restatement of it).  The slice runs the
+    kernels the timed step runs: where the module skips masked synapses at full size,
+    the slice's row threshold is lifted so that it skips them too."""
+    import ltc_layer
+    old_min = ltc_layer.SKIP_MIN_ROWS
+    ltc_layer.SKIP_MIN_ROWS = 0 if skip_zero else old_min
+    try:
+        return _our_parity(cfg, p, dev, skip_zero)
+    finally:
+        ltc_layer.SKIP_MIN_ROWS = old_min
+
+
+def _our_parity(cfg, p, dev, skip_zero):
     import ltc_layer
     from oracle import reference_module as rm
 
@@ -331,6 +343,7 @@ def our_parity(cfg, p, dev):
         m = ltc_layer.TrueLiquidTimeConstant(cfg.D, cfg.H, dt=cfg.dt, ode_unfolds=cfg.U, sparsity=cfg.density,
                                              sensory_sparsity=cfg.sensory_density)
         m.load_state_dict(p)
+        m.skip_zero_synapses = m.skip_zero_synapses and skip_zero
         return m.to(dev)
     if rm.available() is None:
         import logging
@@ -453,7 +466,9 @@ def main():
 
     parity = None
     if rank == 0 and args.parity:
-        parity = our_parity(cfg, p, dev)
+        import ltc_layer
+        # the slice takes the timed step's path: skipping where the step's rows reach the threshold
+        parity = our_parity(cfg, p, dev, bool(args.skip_zero) and Bl * cfg.T >= ltc_layer.SKIP_MIN_ROWS)
     for _ in range(max(3, args.warmup)):
         step(x_dev)
     torch.cuda.synchronize()

@@ -64,6 +64,15 @@ typedef struct {
  * sensory_w_pos != 0 (any pattern; D up to 682, larger D keeps the dense pass); that changes no output
  * beyond summation order and no gradient. */
 #define LTC_FLAG_SKIP_ZERO_SYNAPSES 4
+/* Also skip the zero sensory synapses (sensory_w_pos == 0) in the sensory backward
+ * (no counterpart in the reference, csrc/ltc_kernels.cu:675-950 visits all D*H).
+ * Like the recurrent case, the caller declares the sensory_w_pos gradient unused at
+ * those positions (true for softplus(w) * mask); the four sensory gradients are
+ * written as zero there.  Honoured together with LTC_FLAG_SKIP_ZERO_SYNAPSES when
+ * H <= 64 and the recurrent synapses are skipped.  Capacity (H > 32): within each
+ * chunk of 64 consecutive inputs every input may feed at most 48 nonzero synapses
+ * and every column receive at most 48; beyond it the outputs are NaN. */
+#define LTC_FLAG_SKIP_ZERO_SENSORY (1 << 24)
 /* Bits 8..23 of flags, if nonzero, fix the lean segment length in steps
  * (otherwise it is sized for about 512 MiB of per-unfold state). */
 #define LTC_LEAN_CHUNK_SHIFT 8

@@ -127,6 +127,7 @@ struct Layout {
   size_t saved_floats_v, saved_floats_r;
   bool lean;  // LTC_FLAG_LEAN_SAVE: saved = step-boundary states; the backward recomputes segments
   bool skip_sens;  // LTC_FLAG_SKIP_ZERO_SYNAPSES: the sensory forward visits only sw != 0
+  bool skip_sens_bwd;  // LTC_FLAG_SKIP_ZERO_SENSORY: so does the sensory backward (H <= 64)
   int tc;     // lean segment length in steps
 };
 
@@ -153,6 +154,9 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
   L->skip_sens = (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) && !(d->flags & LTC_FLAG_FORCE_WIDE) &&
                  sens_sparse_fits(d->D);
   L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
+  L->skip_sens_bwd = (d->flags & LTC_FLAG_SKIP_ZERO_SENSORY) && L->rp.sparse && !L->rp.streamed &&
+                     L->rp.HP <= 64;
+  if (L->skip_sens_bwd) plan_sensory_bwd_sparse(L->sp, L->rows, d->D, L->rp.HP, di->sms);
   const size_t tu = (size_t)d->T * d->ode_unfolds;
   L->lean = (d->flags & LTC_FLAG_LEAN_SAVE) != 0;
   L->tc = 0;
@@ -204,6 +208,7 @@ struct BwdBuffers {
   float *xc, *snc, *sdc, *gsnc, *gsdc, *Vc, *Rc, *hs, *ghA, *ghB, *fscratch;
   void* tables;   // sparse path only
   void* stables;  // sensory lists (lean recompute with skip_sens only)
+  void* sbtables;  // sensory backward slot tables (skip_sens_bwd only)
 };
 size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   Carver c(ws);
@@ -221,6 +226,7 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
   b->tables = L.rp.sparse ? c.take<char>(sparse_tables_bytes(HP)) : nullptr;
   b->stables = L.lean && L.skip_sens ? c.take<char>(sens_tables_bytes(d->D, HP)) : nullptr;
+  b->sbtables = L.skip_sens_bwd ? c.take<char>(sens_bwd_tables_bytes(d->D, HP)) : nullptr;
   b->xc = b->snc = b->sdc = b->gsnc = b->gsdc = b->Vc = b->Rc = b->hs = b->ghA = b->ghB = b->fscratch = nullptr;
   if (L.lean) {
     const size_t BH = (size_t)d->B * d->H, tcu = (size_t)L.tc * d->ode_unfolds;
@@ -502,6 +508,11 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
     e = launch_build_sens(pa, b.stables, st);
     if (e != cudaSuccess) return cuda_fail(e, "build_sens");
   }
+  if (b.sbtables) {
+    TimedLaunch tl(LTC_KERNEL_PACK_BWD, st);
+    e = launch_build_sens_slots(pa, b.sbtables, st);
+    if (e != cudaSuccess) return cuda_fail(e, "build_sens_slots");
+  }
 
   Carver sc(const_cast<void*>(saved));
   RecBwdArgs ra{};
@@ -528,7 +539,8 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   sa.part = b.spart; sa.rows = L.rows; sa.D = dims->D; sa.H = dims->H; sa.HP = HP; sa.nsplit = L.sp.nsplit;
   {
     TimedLaunch tl(LTC_KERNEL_SENSORY_BWD, st);
-    e = launch_sensory_bwd(sa, L.sp, b.dxpart, L.rp.tanh_space, st);
+    e = L.skip_sens_bwd ? launch_sensory_bwd_sparse(sa, L.sp, b.sbtables, st)
+                        : launch_sensory_bwd(sa, L.sp, b.dxpart, L.rp.tanh_space, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sensory_bwd");
 
@@ -539,6 +551,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
     fa.skip_w_pos = params->w_pos;
     fa.skip_w_erev = params->w_erev;
   }
+  if (L.skip_sens_bwd) fa.skip_sw = params->sensory_w_pos;
   fa.sens_part = b.spart; fa.nsplit = L.sp.nsplit; fa.dxpart = b.dxpart; fa.nqc = L.sp.nqc; fa.rows = L.rows;
   fa.mu = params->mu; fa.sigma = params->sigma; fa.smu = params->sensory_mu; fa.ssig = params->sensory_sigma;
   fa.serev = params->sensory_erev; fa.sw = params->sensory_w_pos;

@@ -74,6 +74,13 @@ SensBwdPlan plan_sensory_bwd(long long rows, int D, int HP, int num_sms);
 // column sums of g_sn, g_sd taken from the recurrent per-neuron partials (rows 3, 4)
 cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart, bool tanh_space,
                                cudaStream_t st);
+// masked sensory synapses skipped in the backward (H <= 64, LTC_FLAG_SKIP_ZERO_SENSORY;
+// ltc_recurrent_sparse.cu): slot tables per chunk of HP inputs, tanh space
+size_t sens_bwd_tables_bytes(int D, int HP);
+void plan_sensory_bwd_sparse(SensBwdPlan& p, long long rows, int D, int HP, int num_sms);
+cudaError_t launch_build_sens_slots(const struct PackArgs& pa, void* tables, cudaStream_t st);
+cudaError_t launch_sensory_bwd_sparse(const SensBwdArgs& a, const SensBwdPlan& p, const void* tables,
+                                      cudaStream_t st);
 
 // ---- recurrent forward / backward ----------------------------------------
 struct RecFwdArgs {
@@ -158,6 +165,9 @@ struct FinishArgs {
   // sparse path: synapses with w_pos == w_erev == 0 were skipped; their four
   // gradients are written as zero (their partial-slab entries are never written)
   const float* skip_w_pos; const float* skip_w_erev;
+  // sensory synapses with sw == 0 were skipped in the sensory backward: their four
+  // gradients are written as zero
+  const float* skip_sw;
   const float* sens_part;  // [nsplit][4][D*HP]
   int nsplit;
   const float* dxpart;     // [nqc][rows*D] or null

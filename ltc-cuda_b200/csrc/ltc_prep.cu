@@ -130,6 +130,10 @@ __global__ void finish_kernel(FinishArgs a) {
     } else if (i < nrec + nneu + nsen) {
       const long long k = i - nrec - nneu;
       const int d = (int)(k / a.H), q = (int)(k % a.H);
+      if (a.skip_sw && a.skip_sw[k] == 0.f) {
+        a.g_serev[k] = a.g_sw[k] = a.g_smu[k] = a.g_ssig[k] = 0.f;
+        continue;
+      }
       const long long idx = (long long)d * a.HP + q;
       const long long slab = (long long)a.D * a.HP;
       float an = 0.f, ad = 0.f, dz = 0.f, dzx = 0.f;

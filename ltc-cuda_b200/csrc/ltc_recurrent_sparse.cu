@@ -101,7 +101,9 @@ inline SlotTablesView tables_view(void* base, int HP) {
 // column q, list = its nonzero rows p.
 template <int HP>
 __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, const float* __restrict__ w_pos,
-                                                          const float* __restrict__ w_erev, int H) {
+                                                          const float* __restrict__ w_erev, int H, int P) {
+  // rows p < P of a row-major (., H) pattern with row stride H: P = H for the
+  // recurrent matrix, a chunk of at most HP inputs for the sensory one
   constexpr int NPAIR = HP / 2, CAP = HP == 64 ? kCap64 : 32;
   __shared__ uint64_t nz[2][HP];  // [0] bit q of row p; [1] bit p of column q
   __shared__ int cnt[2][HP];
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
     for (int h = 0; h < HP / 32; ++h) {
       const int q = 32 * h + lane;
       const long long j = (long long)p * H + q;
-      const bool on = p < H && q < H && (w_pos[j] != 0.f || w_erev[j] != 0.f);
+      const bool on = p < P && q < H && (w_pos[j] != 0.f || w_erev[j] != 0.f);
       m |= (uint64_t)__ballot_sync(0xffffffffu, on) << (32 * h);
     }
     if (lane == 0) nz[0][p] = m;
@@ -703,6 +705,133 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
   }
 }
 
+
+// ---- sensory backward over the nonzero sensory synapses (H <= 64) -------------
+// The sensory backward is the recurrent backward's synapse pass with the
+// presynaptic neuron p replaced by the input d and no recurrence: for each chunk of
+// HP inputs, slot tables of that chunk of the sensory pattern (build_slots_kernel on
+// rows d0 .. d0 + HP of sw) give every lane its synapses; a CTA = (input chunk, row
+// split) walks its rows in tiles of kSensRows.  Per tile, g_sn / g_sd are staged
+// neuron-major (column q, rows) exactly as the recurrent adjoints, and x row-major as
+// the recurrent states; the 4 gradient sums per synapse stay in registers over the
+// whole row split, dx[row][d] comes out of the lane reduction.  Tanh space as in the
+// dense sensory backward: the -1/4 of a' = -g/4 is folded into the weights, so the
+// raw g_sn / g_sd are staged and the A_n / A_d sums are scaled by -1/4 at the end.
+constexpr int kSensRows = 64;
+
+template <int HP>
+__global__ void __launch_bounds__(side_nt(HP, 0), 1)
+    sens_bwd_sparse(SensBwdArgs a, SlotTablesView tv, size_t chunk_bytes, long long rows_per_split) {
+  using F = SparseBwd<HP>;
+  constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV, kTPC = F::TPC, R = kSensRows;
+  using LR = LaneReduce<kTPC, 2 * kSB>;
+  extern __shared__ __align__(16) float smem[];
+  const int S = 4 * neuron_stride4(R);
+  float* GN = smem;              // [2][HP][S]  g_sn, neuron-major
+  float* GD = GN + 2 * HP * S;   // [2][HP][S]  g_sd
+  float* XS = GD + 2 * HP * S;   // [2][R][LDV] x of the chunk's inputs
+  const int chunk = blockIdx.x, split = blockIdx.y;
+  {  // this chunk's tables
+    const size_t o = (size_t)chunk * chunk_bytes;
+    tv.bneu = reinterpret_cast<int*>(reinterpret_cast<char*>(tv.bneu) + o);
+    tv.bk = reinterpret_cast<int*>(reinterpret_cast<char*>(tv.bk) + o);
+    tv.bidx = reinterpret_cast<int*>(reinterpret_cast<char*>(tv.bidx) + o);
+    tv.overflow = reinterpret_cast<int*>(reinterpret_cast<char*>(tv.overflow) + o);
+  }
+  const int d0 = chunk * HP;
+  const int tid = threadIdx.x, lane = tid & 31, c = tid / kTPC;
+  const int D = a.D, H = a.H;
+  const int kw = tv.bk[tid / 32];
+  const float bad = *tv.overflow ? __int_as_float(0x7fc00000) : 0.f;  // NaN poisons every output
+  const int rowA = tv.bneu[2 * c], rowB = tv.bneu[2 * c + 1];
+
+  F f;
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int j = 0; j < KM; ++j) {
+      const int base = (tid * 2 + r) * KM + j;
+      const int ix = tv.bidx[base];  // column q
+      const int d = d0 + (r ? rowB : rowA);
+      float4 pk = (ix < 0 || d >= D) ? make_float4(0.f, 0.f, 0.f, 0.f) : a.spack[(long long)d * a.HP + ix];
+      pk.x = -pk.x;  // gate argument -z/2
+      pk.y = -pk.y;
+      pk.z *= -0.25f;  // a' = -g/4 folded into the weights
+      pk.w *= -0.25f;
+      f.sl2[r][j] = make_float2(pk.x, pk.x);
+      f.nm2[r][j] = make_float2(pk.y, pk.y);
+      f.wp2[r][j] = make_float2(pk.z, pk.z);
+      f.we2[r][j] = make_float2(pk.w, pk.w);
+      f.Gwe[r][j] = f.Gwp[r][j] = f.Gdz[r][j] = f.Gdzv[r][j] = make_float2(bad, bad);
+      f.off.set(r * KM + j, (uint32_t)((ix < 0 ? 0 : ix) * S * 4));
+    }
+  const int own = LR::own_base(lane);
+  const int orow = own / kSB, osmp = own % kSB;
+  const int p = orow ? rowB : rowA;
+  const bool pvalid = d0 + p < D;
+  const bool writer = LR::writer(lane);
+  const long long r_begin = split * rows_per_split;
+  const long long r_end = min(a.rows, r_begin + rows_per_split);
+
+  auto stage = [&](long long rt, int buf) {
+    const int nr = (int)min((long long)R, r_end - rt);
+    float* gn = GN + buf * HP * S;
+    float* gd = GD + buf * HP * S;
+    float* xs = XS + buf * R * LDV;
+    for (int i = tid; i < R * HP; i += NT) {
+      const int r = i / HP, q = i % HP;  // consecutive threads read consecutive columns of a row
+      const bool ok = r < nr && q < H;
+      const long long src = ok ? (rt + r) * H + q : 0;
+      cp_async4_zfill(gn + q * S + r, a.gsn + src, ok);
+      cp_async4_zfill(gd + q * S + r, a.gsd + src, ok);
+      const bool okx = r < nr && d0 + q < D;
+      cp_async4_zfill(xs + r * LDV + q, a.x + (okx ? (rt + r) * D + d0 + q : 0), okx);
+    }
+    cp_async_commit();
+  };
+  if (r_begin < r_end) stage(r_begin, 0);
+  int buf = 0;
+  for (long long rt = r_begin; rt < r_end; rt += R, buf ^= 1) {
+    const int nr = (int)min((long long)R, r_end - rt);
+    cp_async_wait_all();
+    __syncthreads();  // tile rt landed; the other buffer is free again
+    if (rt + R < r_end) stage(rt + R, buf ^ 1);
+    const char* an_s = reinterpret_cast<const char*>(GN + buf * HP * S);
+    const char* ad_s = reinterpret_cast<const char*>(GD + buf * HP * S);
+    const float* xs = XS + buf * R * LDV;
+    const int nblk = (nr + kSB - 1) / kSB;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const float* vb = xs + blk * kSB * LDV;
+      const float4 vr[2] = {make_float4(vb[rowA], vb[LDV + rowA], vb[2 * LDV + rowA], vb[3 * LDV + rowA]),
+                            make_float4(vb[rowB], vb[LDV + rowB], vb[2 * LDV + rowB], vb[3 * LDV + rowB])};
+      float acc[1][2 * kSB];
+      dispatch_kk<KM>(kw, [&](auto K1, auto K2) {
+        f.template pass<decltype(K1)::value, decltype(K2)::value>(an_s + 16 * blk, ad_s + 16 * blk, vr, acc);
+      });
+      LR::template run<1>(acc, lane);
+      const int s = blk * kSB + osmp;
+      if (writer && pvalid && s < nr) a.dx[(rt + s) * D + d0 + p] = -2.0f * acc[0][0] + bad;  // sl holds -sigma/2
+    }
+  }
+  // synapse partials at their dense positions (skipped synapses are never written)
+  const long long slab = (long long)D * a.HP;
+  float* part = a.part + (long long)split * 4 * slab;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int d = d0 + (r ? rowB : rowA);
+#pragma unroll
+    for (int j = 0; j < KM; ++j) {
+      const int qi = tv.bidx[(tid * 2 + r) * KM + j];
+      if (qi < 0 || d >= D) continue;
+      const long long idx = (long long)d * a.HP + qi;
+      part[idx] = -0.25f * (f.Gwe[r][j].x + f.Gwe[r][j].y);
+      part[slab + idx] = -0.25f * (f.Gwp[r][j].x + f.Gwp[r][j].y);
+      part[2 * slab + idx] = f.Gdz[r][j].x + f.Gdz[r][j].y;
+      part[3 * slab + idx] = f.Gdzv[r][j].x + f.Gdzv[r][j].y;
+    }
+  }
+}
+
 template <typename K, typename Args>
 cudaError_t launch_plain(K kernel, const Args& a, const SlotTablesView& tv, int grid, int threads, size_t smem,
                          cudaStream_t st) {
@@ -752,13 +881,77 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
   p.tanh_space = true;
 }
 
+
+// ---- sensory backward (skipped sensory synapses, H <= 64) ------------------------
+size_t sens_bwd_tables_bytes(int D, int HP) {
+  size_t at[7];
+  return (size_t)((D + HP - 1) / HP) * tables_layout(HP, at);
+}
+
+void plan_sensory_bwd_sparse(SensBwdPlan& p, long long rows, int D, int HP, int num_sms) {
+  const int nchunk = (D + HP - 1) / HP;
+  int ns = num_sms / nchunk;
+  if (ns < 1) ns = 1;
+  const long long max_split = (rows + kSensRows - 1) / kSensRows;
+  if (ns > max_split) ns = (int)(max_split > 0 ? max_split : 1);
+  p.qc = HP;
+  p.nqc = 1;
+  p.dpc = HP;
+  p.ndc = nchunk;
+  p.nsplit = ns;
+  p.part_floats = (size_t)ns * 4 * D * HP;
+  p.dxpart_floats = 0;
+}
+
+cudaError_t launch_build_sens_slots(const PackArgs& pa, void* tables, cudaStream_t st) {
+  size_t at[7];
+  const size_t cb = tables_layout(pa.HP, at);
+  for (int ch = 0; ch * pa.HP < pa.D; ++ch) {
+    const SlotTablesView tv = tables_view(static_cast<char*>(tables) + ch * cb, pa.HP);
+    const float* w = pa.sw + (long long)ch * pa.HP * pa.H;
+    const int P = pa.D - ch * pa.HP < pa.HP ? pa.D - ch * pa.HP : pa.HP;
+    if (pa.HP == 64)
+      build_slots_kernel<64><<<1, 256, 0, st>>>(tv, w, w, pa.H, P);
+    else
+      build_slots_kernel<32><<<1, 256, 0, st>>>(tv, w, w, pa.H, P);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_sensory_bwd_sparse(const SensBwdArgs& a, const SensBwdPlan& p, const void* tables,
+                                      cudaStream_t st) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.HP != 32 && a.HP != 64) return cudaErrorInvalidValue;
+  long long rps = (a.rows + p.nsplit - 1) / p.nsplit;
+  rps = (rps + kSensRows - 1) / kSensRows * kSensRows;
+  size_t at[7];
+  const size_t cb = tables_layout(a.HP, at);
+  const SlotTablesView tv = tables_view(const_cast<void*>(tables), a.HP);
+  const int S = 4 * neuron_stride4(kSensRows);
+  const size_t smem = ((size_t)4 * a.HP * S + (size_t)2 * kSensRows * (a.HP + 4)) * sizeof(float);
+  const dim3 grid(p.ndc, p.nsplit);
+  cudaError_t e;
+  if (a.HP == 64) {
+    e = cudaFuncSetAttribute(sens_bwd_sparse<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    sens_bwd_sparse<64><<<grid, side_nt(64, 0), smem, st>>>(a, tv, cb, rps);
+  } else {
+    e = cudaFuncSetAttribute(sens_bwd_sparse<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    sens_bwd_sparse<32><<<grid, side_nt(32, 0), smem, st>>>(a, tv, cb, rps);
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st) {
   if (pa.HP > 64) return launch_build_csp(pa, tables, st);
   const SlotTablesView tv = tables_view(tables, pa.HP);
   if (pa.HP == 64)
-    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H);
+    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H, pa.H);
   else
-    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H);
+    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H, pa.H);
   return cudaGetLastError();
 }
 

@@ -42,6 +42,7 @@ LIB_PATH = os.environ.get("LTC_SM100_LIB", os.path.join(_HERE, "libltc_sm100.so"
 LTC_FLAG_FORCE_WIDE = 1
 LTC_FLAG_LEAN_SAVE = 2
 LTC_FLAG_SKIP_ZERO_SYNAPSES = 4
+LTC_FLAG_SKIP_ZERO_SENSORY = 1 << 24
 LTC_LEAN_CHUNK_SHIFT = 8
 
 
@@ -196,15 +197,27 @@ class skip_zero_synapses:
     (``LTC_FLAG_SKIP_ZERO_SYNAPSES``).  The solver's gradients of ``w_pos``, ``w_erev``,
     ``mu`` and ``sigma`` are then zero at those positions instead of the dense values --
     use it only where those entries are discarded, as when ``w_pos = softplus(w) * mask``
-    (the module's transforms).  Other outputs are unchanged."""
+    (the module's transforms).  Other outputs are unchanged.
 
-    def __init__(self, on: bool = True):
+    ``sensory=True`` (with ``on``) also skips the sensory synapses whose
+    ``sensory_w_pos`` is zero in the sensory backward (``LTC_FLAG_SKIP_ZERO_SENSORY``,
+    H <= 64): the four sensory gradients are then zero at those positions -- again only
+    for callers that discard them, as ``sensory_w_pos = softplus(w) * mask`` does.
+    Check the pattern with :func:`skip_zero_sensory_fits` first."""
+
+    def __init__(self, on: bool = True, sensory: bool = False):
         self.on = bool(on)
+        self.sensory = bool(on and sensory)
 
     def __enter__(self):
         self.prev = getattr(_call_flags, "extra", 0)
-        _call_flags.extra = (self.prev | LTC_FLAG_SKIP_ZERO_SYNAPSES) if self.on else \
-            (self.prev & ~LTC_FLAG_SKIP_ZERO_SYNAPSES)
+        both = LTC_FLAG_SKIP_ZERO_SYNAPSES | LTC_FLAG_SKIP_ZERO_SENSORY
+        flags = self.prev & ~both
+        if self.on:
+            flags |= LTC_FLAG_SKIP_ZERO_SYNAPSES
+        if self.sensory:
+            flags |= LTC_FLAG_SKIP_ZERO_SENSORY
+        _call_flags.extra = flags
         return self
 
     def __exit__(self, *exc):
@@ -250,6 +263,24 @@ def skip_zero_synapses_fits(mask: torch.Tensor) -> bool:
     if H <= 64:
         return int(torch.maximum(nz.sum(0).max(), nz.sum(1).max()).item()) <= SKIP_MAX_SYNAPSES_PER_NEURON
     return _wide_fits(nz)
+
+
+def skip_zero_sensory_fits(smask: torch.Tensor) -> bool:
+    """True when the (D, H) sensory pattern fits the sensory backward's skipping kernel:
+    H <= 64 and, for H > 32, at most 48 nonzero synapses per input and per column
+    inside every chunk of 64 consecutive inputs."""
+    D, H = smask.shape
+    if H > 64:
+        return False
+    if H <= 32:
+        return True
+    nz = (smask != 0)
+    for d0 in range(0, D, 64):
+        blk = nz[d0:d0 + 64]
+        if int(blk.sum(1).max().item()) > SKIP_MAX_SYNAPSES_PER_NEURON or \
+                int(blk.sum(0).max().item()) > SKIP_MAX_SYNAPSES_PER_NEURON:
+            return False
+    return True
 
 
 def _call_flags_now() -> int:

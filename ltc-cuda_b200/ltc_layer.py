@@ -133,7 +133,8 @@ class TrueLiquidTimeConstant(nn.Module):
         # multiplied by zero on the way to w and erev, so the solver may skip them
         # (small problems stay dense: rebuilding the slot tables costs more than it saves)
         skip = self.skip_zero_synapses and B * T >= SKIP_MIN_ROWS and self._skip_fits()
-        with ltc_cuda.skip_zero_synapses(skip):
+        # sensory_w_pos = softplus(sensory_w) * mask: the same holds for the sensory synapses
+        with ltc_cuda.skip_zero_synapses(skip, sensory=skip and self._skip_sensory_fits()):
             outputs, state = _solver(x, state, w_pos, w_erev, self.mu, self.sigma, self.sensory_mu,
                                      self.sensory_sigma, self.sensory_erev, sensory_w_pos, cm_t, gleak_pos,
                                      self.vleak, self.ode_unfolds, self.epsilon)
@@ -148,6 +149,16 @@ class TrueLiquidTimeConstant(nn.Module):
             self._skip_ok = ltc_cuda.skip_zero_synapses_fits(m)
             self._skip_key = key
         return self._skip_ok
+
+    def _skip_sensory_fits(self) -> bool:
+        """Whether the sensory backward's skipping kernel can hold the sensory mask
+        (checked once per mask version)."""
+        m = self.sensory_sparsity_mask
+        key = (m.data_ptr(), m._version, tuple(m.shape))
+        if getattr(self, "_sskip_key", None) != key:
+            self._sskip_ok = bool((m == 0).any().item()) and ltc_cuda.skip_zero_sensory_fits(m)
+            self._sskip_key = key
+        return self._sskip_ok
 
     def train(self, mode: bool = True):
         if mode:

@@ -258,3 +258,58 @@ def test_sensory_lists_vs_oracle(D):
     inp = {k: v.detach() for k, v in orc.module_preamble(p, x, 1 / 30, 3).items()}
     inp["state"] = torch.randn(7, H, generator=g) * 0.3
     _check(inp, 3, torch.randn(7, 6, H, generator=g), torch.randn(7, H, generator=g), f"D{D}")
+
+
+# ---- sensory backward over the nonzero sensory synapses (LTC_FLAG_SKIP_ZERO_SENSORY) --
+
+def _check_sensory(inp, U, gout, gh, ctx):
+    with ltc_cuda.skip_zero_synapses(sensory=True):
+        out, h, g = cuda_solver(inp, U, 1e-8, gout=gout, gh=gh)
+    ro, rh, rg = oracle_solver(inp, U, 1e-8, gout=gout, gh=gh)
+    assert (out.cpu() - ro.cpu()).abs().max().item() < FWD_ATOL, ctx
+    rg = _expect_masked({k: v.cpu() for k, v in rg.items()}, {k: v.cpu() for k, v in inp.items()})
+    zs = inp["sensory_w_pos"].cpu() == 0
+    for k in ("sensory_w_pos", "sensory_erev", "sensory_mu", "sensory_sigma"):
+        rg[k] = torch.where(zs, torch.zeros_like(rg[k]), rg[k])
+        assert float(g[k].cpu()[zs].abs().max().item() if zs.any() else 0.0) == 0.0, f"{ctx} {k} skipped != 0"
+    assert_grads_close(g, rg, ctx=ctx)
+    for k in FN:
+        assert rel_err(g[k], rg[k]) < 2e-3, f"{ctx} {k}: {rel_err(g[k], rg[k]):.2e}"
+
+
+@pytest.mark.parametrize("D,H,sdens,B,T", [(128, 64, 0.5, 9, 70), (40, 64, 0.3, 5, 20), (100, 48, 0.5, 3, 33),
+                                           (70, 32, 1.0, 4, 40), (16, 17, 0.5, 6, 9)])
+def test_sensory_backward_vs_oracle(D, H, sdens, B, T):
+    """Ragged input chunks (D not a multiple of 64), rows not a multiple of the tile,
+    H <= 32 (any pattern) and a dense sensory mask at H = 32."""
+    p = synth.make_params(D, H, 0.5, sdens, seed=D + H)
+    g = torch.Generator().manual_seed(D * H)
+    x = torch.randn(B, T, D, generator=g)
+    inp = {k: v.detach() for k, v in orc.module_preamble(p, x, 1 / 30, 3).items()}
+    inp["state"] = torch.randn(B, H, generator=g) * 0.3
+    assert ltc_cuda.skip_zero_sensory_fits(p["sensory_sparsity_mask"])
+    _check_sensory(inp, 3, torch.randn(B, T, H, generator=g), torch.randn(B, H, generator=g), f"D{D} H{H}")
+
+
+def test_sensory_capacity_and_module():
+    """The fits check mirrors the kernel's capacity; the module turns the sensory path on
+    only where it fits, and its gradients then equal the dense path's."""
+    d, q = torch.arange(128)[:, None], torch.arange(64)[None, :]
+    m = (((q - d) % 64) < 48).float()  # every input feeds 48 columns, every column gets 48 per chunk
+    assert ltc_cuda.skip_zero_sensory_fits(m)
+    m[3, (3 + 48) % 64] = 1.0  # input 3 feeds 49 columns
+    assert not ltc_cuda.skip_zero_sensory_fits(m)
+    torch.manual_seed(5)
+    mod = ltc_layer.TrueLiquidTimeConstant(72, 64, sparsity=0.4, sensory_sparsity=0.5).cuda()
+    assert mod._skip_sensory_fits()
+    x = torch.randn(128, 40, 72, device="cuda")
+    grads = []
+    for skip in (True, False):
+        mod.skip_zero_synapses = skip
+        mod.zero_grad()
+        out, (h, _) = mod(x)
+        (out.sum() + h.square().sum()).backward()
+        grads.append({n: q.grad.clone() for n, q in mod.named_parameters()})
+    for n in grads[0]:
+        a, b = grads[0][n], grads[1][n]
+        assert rel_err(a, b) < 1e-5, f"{n}: {rel_err(a, b):.3e}"
