@@ -160,10 +160,10 @@ __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTab
         float sn[RPL], sd[RPL];
 #pragma unroll
         for (int i = 0; i < RPL; ++i) sn[i] = sd[i] = 0.f;
-        auto visit = [&](int k) {
+        auto visit = [&](int k, int xo) {  // xo: the entry's input d times TR
           const float4 w = lcs[k];
           float xv[RPL];
-          RowVec<RPL>::load(xt + lis[k] * TR, xv);
+          RowVec<RPL>::load(xt + xo, xv);
 #pragma unroll
           for (int i = 0; i < RPL; ++i) {
             const float th = tanh_approx(fmaf(w.x, xv[i], w.y));
@@ -179,18 +179,19 @@ __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTab
             const int k = j * 32 + lane;
             if (k < m) {
               lcs[k] = lc[base + k];
-              lis[k] = li[base + k];
+              lis[k] = li[base + k] * TR;
             }
           }
           __syncwarp();
           int k = 0;
           for (; k + 3 < m; k += 4) {
-            visit(k);
-            visit(k + 1);
-            visit(k + 2);
-            visit(k + 3);
+            const int4 xo = *reinterpret_cast<const int4*>(lis + k);  // four offsets, one load
+            visit(k, xo.x);
+            visit(k + 1, xo.y);
+            visit(k + 2, xo.z);
+            visit(k + 3, xo.w);
           }
-          for (; k < m; ++k) visit(k);
+          for (; k < m; ++k) visit(k, lis[k]);
         }
         const float2 cw = tv.cw[q];
 #pragma unroll
