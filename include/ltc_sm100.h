@@ -68,10 +68,11 @@ typedef struct {
  * (no counterpart in the reference, csrc/ltc_kernels.cu:675-950 visits all D*H).
  * Like the recurrent case, the caller declares the sensory_w_pos gradient unused at
  * those positions (true for softplus(w) * mask); the four sensory gradients are
- * written as zero there.  Honoured together with LTC_FLAG_SKIP_ZERO_SYNAPSES when
- * H <= 64 and the recurrent synapses are skipped.  Capacity (H > 32): within each
- * chunk of 64 consecutive inputs every input may feed at most 48 nonzero synapses
- * and every column receive at most 48; beyond it the outputs are NaN. */
+ * written as zero there.  Honoured together with LTC_FLAG_SKIP_ZERO_SYNAPSES where
+ * the recurrent synapses are skipped (H <= 64, 128 < H <= 512).  Capacity (H > 32):
+ * within each block of 64 consecutive inputs x 64 consecutive columns every input
+ * may feed at most 48 nonzero synapses and every column receive at most 48; beyond
+ * it the outputs are NaN. */
 #define LTC_FLAG_SKIP_ZERO_SENSORY (1 << 24)
 /* Bits 8..23 of flags, if nonzero, fix the lean segment length in steps
  * (otherwise it is sized for about 512 MiB of per-unfold state). */

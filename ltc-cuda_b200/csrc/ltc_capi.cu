@@ -154,9 +154,8 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
   L->skip_sens = (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) && !(d->flags & LTC_FLAG_FORCE_WIDE) &&
                  sens_sparse_fits(d->D);
   L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
-  L->skip_sens_bwd = (d->flags & LTC_FLAG_SKIP_ZERO_SENSORY) && L->rp.sparse && !L->rp.streamed &&
-                     L->rp.HP <= 64;
-  if (L->skip_sens_bwd) plan_sensory_bwd_sparse(L->sp, L->rows, d->D, L->rp.HP, di->sms);
+  L->skip_sens_bwd = (d->flags & LTC_FLAG_SKIP_ZERO_SENSORY) && L->rp.sparse && L->rp.tanh_space;
+  if (L->skip_sens_bwd) plan_sensory_bwd_sparse(L->sp, L->rows, d->D, d->H, L->rp.HP, di->sms);
   const size_t tu = (size_t)d->T * d->ode_unfolds;
   L->lean = (d->flags & LTC_FLAG_LEAN_SAVE) != 0;
   L->tc = 0;
@@ -226,7 +225,7 @@ size_t carve_bwd(const LtcDims* d, const Layout& L, void* ws, BwdBuffers* b) {
   b->scratch = L.rp.scratch_bwd ? c.take<float>(L.rp.scratch_bwd) : nullptr;
   b->tables = L.rp.sparse ? c.take<char>(sparse_tables_bytes(HP)) : nullptr;
   b->stables = L.lean && L.skip_sens ? c.take<char>(sens_tables_bytes(d->D, HP)) : nullptr;
-  b->sbtables = L.skip_sens_bwd ? c.take<char>(sens_bwd_tables_bytes(d->D, HP)) : nullptr;
+  b->sbtables = L.skip_sens_bwd ? c.take<char>(sens_bwd_tables_bytes(d->D, d->H, HP)) : nullptr;
   b->xc = b->snc = b->sdc = b->gsnc = b->gsdc = b->Vc = b->Rc = b->hs = b->ghA = b->ghB = b->fscratch = nullptr;
   if (L.lean) {
     const size_t BH = (size_t)d->B * d->H, tcu = (size_t)L.tc * d->ode_unfolds;
@@ -539,7 +538,7 @@ int ltc_backward(const LtcDims* dims, const LtcParams* params, const float* x, c
   sa.part = b.spart; sa.rows = L.rows; sa.D = dims->D; sa.H = dims->H; sa.HP = HP; sa.nsplit = L.sp.nsplit;
   {
     TimedLaunch tl(LTC_KERNEL_SENSORY_BWD, st);
-    e = L.skip_sens_bwd ? launch_sensory_bwd_sparse(sa, L.sp, b.sbtables, st)
+    e = L.skip_sens_bwd ? launch_sensory_bwd_sparse(sa, L.sp, b.sbtables, b.dxpart, st)
                         : launch_sensory_bwd(sa, L.sp, b.dxpart, L.rp.tanh_space, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sensory_bwd");

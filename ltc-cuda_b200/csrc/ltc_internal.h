@@ -74,13 +74,14 @@ SensBwdPlan plan_sensory_bwd(long long rows, int D, int HP, int num_sms);
 // column sums of g_sn, g_sd taken from the recurrent per-neuron partials (rows 3, 4)
 cudaError_t launch_sensory_bwd(const SensBwdArgs& a, const SensBwdPlan& p, float* dxpart, bool tanh_space,
                                cudaStream_t st);
-// masked sensory synapses skipped in the backward (H <= 64, LTC_FLAG_SKIP_ZERO_SENSORY;
-// ltc_recurrent_sparse.cu): slot tables per chunk of HP inputs, tanh space
-size_t sens_bwd_tables_bytes(int D, int HP);
-void plan_sensory_bwd_sparse(SensBwdPlan& p, long long rows, int D, int HP, int num_sms);
-cudaError_t launch_build_sens_slots(const struct PackArgs& pa, void* tables, cudaStream_t st);
+// masked sensory synapses skipped in the backward (LTC_FLAG_SKIP_ZERO_SENSORY, any
+// skipping recurrent path; ltc_recurrent_sparse.cu): slot tables per 64 x 64 block
+// (32 x 32 for H <= 32) of the sensory pattern, tanh space
+size_t sens_bwd_tables_bytes(int D, int H, int HP);
+void plan_sensory_bwd_sparse(SensBwdPlan& p, long long rows, int D, int H, int HP, int num_sms);
+cudaError_t launch_build_sens_slots(const PackArgs& pa, void* tables, cudaStream_t st);
 cudaError_t launch_sensory_bwd_sparse(const SensBwdArgs& a, const SensBwdPlan& p, const void* tables,
-                                      cudaStream_t st);
+                                      float* dxpart, cudaStream_t st);
 
 // ---- recurrent forward / backward ----------------------------------------
 struct RecFwdArgs {

@@ -101,10 +101,28 @@ inline SlotTablesView tables_view(void* base, int HP) {
 // column q, list = its nonzero rows p.
 template <int HP>
 __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, const float* __restrict__ w_pos,
-                                                          const float* __restrict__ w_erev, int H, int P) {
-  // rows p < P of a row-major (., H) pattern with row stride H: P = H for the
-  // recurrent matrix, a chunk of at most HP inputs for the sensory one
+                                                          const float* __restrict__ w_erev, int ld, int rows,
+                                                          int cols, int nqc, size_t chunk_bytes) {
+  // One CTA per HP x HP block of a row-major (rows, cols) pattern with row stride ld,
+  // blocks numbered (row block, column block) with nqc column blocks; block b's tables
+  // sit chunk_bytes * b into the table area.  The recurrent matrix is one block
+  // (rows = cols = ld = H); the sensory one (D, H) is cut into blocks for its backward.
   constexpr int NPAIR = HP / 2, CAP = HP == 64 ? kCap64 : 32;
+  const int p0 = (blockIdx.x / nqc) * HP, q0 = (blockIdx.x % nqc) * HP;
+  const int P = min(HP, rows - p0), Q = min(HP, cols - q0);
+  w_pos += (long long)p0 * ld + q0;
+  w_erev += (long long)p0 * ld + q0;
+  if (blockIdx.x) {
+    const size_t o = (size_t)blockIdx.x * chunk_bytes;
+    auto sh = [o](int* ptr) { return reinterpret_cast<int*>(reinterpret_cast<char*>(ptr) + o); };
+    tv.fneu = sh(tv.fneu);
+    tv.fk = sh(tv.fk);
+    tv.fidx = sh(tv.fidx);
+    tv.bneu = sh(tv.bneu);
+    tv.bk = sh(tv.bk);
+    tv.bidx = sh(tv.bidx);
+    tv.overflow = sh(tv.overflow);
+  }
   __shared__ uint64_t nz[2][HP];  // [0] bit q of row p; [1] bit p of column q
   __shared__ int cnt[2][HP];
   __shared__ int order[2][HP];    // neurons by count, descending
@@ -117,8 +135,8 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
 #pragma unroll
     for (int h = 0; h < HP / 32; ++h) {
       const int q = 32 * h + lane;
-      const long long j = (long long)p * H + q;
-      const bool on = p < P && q < H && (w_pos[j] != 0.f || w_erev[j] != 0.f);
+      const long long j = (long long)p * ld + q;
+      const bool on = p < P && q < Q && (w_pos[j] != 0.f || w_erev[j] != 0.f);
       m |= (uint64_t)__ballot_sync(0xffffffffu, on) << (32 * h);
     }
     if (lane == 0) nz[0][p] = m;
@@ -706,12 +724,14 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
 }
 
 
-// ---- sensory backward over the nonzero sensory synapses (H <= 64) -------------
+// ---- sensory backward over the nonzero sensory synapses -------------------------
 // The sensory backward is the recurrent backward's synapse pass with the
-// presynaptic neuron p replaced by the input d and no recurrence: for each chunk of
-// HP inputs, slot tables of that chunk of the sensory pattern (build_slots_kernel on
-// rows d0 .. d0 + HP of sw) give every lane its synapses; a CTA = (input chunk, row
-// split) walks its rows in tiles of kSensRows.  Per tile, g_sn / g_sd are staged
+// presynaptic neuron p replaced by the input d and no recurrence.  The (D, H) sensory
+// pattern is cut into HP x HP blocks (HP = 32 for H <= 32, else 64; nqc column
+// blocks); each block's slot tables (build_slots_kernel) give every lane its synapses,
+// and a CTA = (block, row split) walks its rows in tiles of kSensRows.  With more than
+// one column block, each writes its own dx partial, summed in a fixed order by the
+// finish kernel.  Per tile, g_sn / g_sd are staged
 // neuron-major (column q, rows) exactly as the recurrent adjoints, and x row-major as
 // the recurrent states; the 4 gradient sums per synapse stay in registers over the
 // whole row split, dx[row][d] comes out of the lane reduction.  Tanh space as in the
@@ -721,7 +741,8 @@ constexpr int kSensRows = 64;
 
 template <int HP>
 __global__ void __launch_bounds__(side_nt(HP, 0), 1)
-    sens_bwd_sparse(SensBwdArgs a, SlotTablesView tv, size_t chunk_bytes, long long rows_per_split) {
+    sens_bwd_sparse(SensBwdArgs a, SlotTablesView tv, size_t chunk_bytes, long long rows_per_split, int nqc,
+                    float* dxpart) {
   using F = SparseBwd<HP>;
   constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV, kTPC = F::TPC, R = kSensRows;
   using LR = LaneReduce<kTPC, 2 * kSB>;
@@ -738,7 +759,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
     tv.bidx = reinterpret_cast<int*>(reinterpret_cast<char*>(tv.bidx) + o);
     tv.overflow = reinterpret_cast<int*>(reinterpret_cast<char*>(tv.overflow) + o);
   }
-  const int d0 = chunk * HP;
+  const int d0 = (chunk / nqc) * HP, q0 = (chunk % nqc) * HP;
   const int tid = threadIdx.x, lane = tid & 31, c = tid / kTPC;
   const int D = a.D, H = a.H;
   const int kw = tv.bk[tid / 32];
@@ -753,7 +774,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
       const int base = (tid * 2 + r) * KM + j;
       const int ix = tv.bidx[base];  // column q
       const int d = d0 + (r ? rowB : rowA);
-      float4 pk = (ix < 0 || d >= D) ? make_float4(0.f, 0.f, 0.f, 0.f) : a.spack[(long long)d * a.HP + ix];
+      float4 pk = (ix < 0 || d >= D) ? make_float4(0.f, 0.f, 0.f, 0.f) : a.spack[(long long)d * a.HP + q0 + ix];
       pk.x = -pk.x;  // gate argument -z/2
       pk.y = -pk.y;
       pk.z *= -0.25f;  // a' = -g/4 folded into the weights
@@ -780,8 +801,8 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
     float* xs = XS + buf * R * LDV;
     for (int i = tid; i < R * HP; i += NT) {
       const int r = i / HP, q = i % HP;  // consecutive threads read consecutive columns of a row
-      const bool ok = r < nr && q < H;
-      const long long src = ok ? (rt + r) * H + q : 0;
+      const bool ok = r < nr && q0 + q < H;
+      const long long src = ok ? (rt + r) * H + q0 + q : 0;
       cp_async4_zfill(gn + q * S + r, a.gsn + src, ok);
       cp_async4_zfill(gd + q * S + r, a.gsd + src, ok);
       const bool okx = r < nr && d0 + q < D;
@@ -810,7 +831,12 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
       });
       LR::template run<1>(acc, lane);
       const int s = blk * kSB + osmp;
-      if (writer && pvalid && s < nr) a.dx[(rt + s) * D + d0 + p] = -2.0f * acc[0][0] + bad;  // sl holds -sigma/2
+      if (writer && pvalid && s < nr) {
+        const float v = -2.0f * acc[0][0] + bad;  // sl holds -sigma/2
+        const long long o = (rt + s) * D + d0 + p;
+        if (nqc == 1) a.dx[o] = v;
+        else dxpart[(long long)(chunk % nqc) * a.rows * D + o] = v;
+      }
     }
   }
   // synapse partials at their dense positions (skipped synapses are never written)
@@ -823,7 +849,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
     for (int j = 0; j < KM; ++j) {
       const int qi = tv.bidx[(tid * 2 + r) * KM + j];
       if (qi < 0 || d >= D) continue;
-      const long long idx = (long long)d * a.HP + qi;
+      const long long idx = (long long)d * a.HP + q0 + qi;
       part[idx] = -0.25f * (f.Gwe[r][j].x + f.Gwe[r][j].y);
       part[slab + idx] = -0.25f * (f.Gwp[r][j].x + f.Gwp[r][j].y);
       part[2 * slab + idx] = f.Gdz[r][j].x + f.Gdz[r][j].y;
@@ -882,65 +908,74 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
 }
 
 
-// ---- sensory backward (skipped sensory synapses, H <= 64) ------------------------
-size_t sens_bwd_tables_bytes(int D, int HP) {
-  size_t at[7];
-  return (size_t)((D + HP - 1) / HP) * tables_layout(HP, at);
+// ---- sensory backward (skipped sensory synapses) ---------------------------------
+// block width of the sensory backward's slot tables: 32 for HP = 32, else 64
+static inline int sens_bh(int HP) { return HP == 32 ? 32 : 64; }
+
+static inline void sens_blocks(int D, int H, int HP, int* ndc, int* nqc) {
+  const int bh = sens_bh(HP);
+  *ndc = (D + bh - 1) / bh;
+  *nqc = (H + bh - 1) / bh;
 }
 
-void plan_sensory_bwd_sparse(SensBwdPlan& p, long long rows, int D, int HP, int num_sms) {
-  const int nchunk = (D + HP - 1) / HP;
-  int ns = num_sms / nchunk;
+size_t sens_bwd_tables_bytes(int D, int H, int HP) {
+  int ndc, nqc;
+  sens_blocks(D, H, HP, &ndc, &nqc);
+  size_t at[7];
+  return (size_t)ndc * nqc * tables_layout(sens_bh(HP), at);
+}
+
+void plan_sensory_bwd_sparse(SensBwdPlan& p, long long rows, int D, int H, int HP, int num_sms) {
+  int ndc, nqc;
+  sens_blocks(D, H, HP, &ndc, &nqc);
+  int ns = num_sms / (ndc * nqc);
   if (ns < 1) ns = 1;
   const long long max_split = (rows + kSensRows - 1) / kSensRows;
   if (ns > max_split) ns = (int)(max_split > 0 ? max_split : 1);
-  p.qc = HP;
-  p.nqc = 1;
-  p.dpc = HP;
-  p.ndc = nchunk;
+  p.qc = sens_bh(HP);
+  p.nqc = nqc;
+  p.dpc = sens_bh(HP);
+  p.ndc = ndc;
   p.nsplit = ns;
   p.part_floats = (size_t)ns * 4 * D * HP;
-  p.dxpart_floats = 0;
+  p.dxpart_floats = nqc > 1 ? (size_t)nqc * rows * D : 0;
 }
 
 cudaError_t launch_build_sens_slots(const PackArgs& pa, void* tables, cudaStream_t st) {
+  int ndc, nqc;
+  sens_blocks(pa.D, pa.H, pa.HP, &ndc, &nqc);
+  const int bh = sens_bh(pa.HP);
   size_t at[7];
-  const size_t cb = tables_layout(pa.HP, at);
-  for (int ch = 0; ch * pa.HP < pa.D; ++ch) {
-    const SlotTablesView tv = tables_view(static_cast<char*>(tables) + ch * cb, pa.HP);
-    const float* w = pa.sw + (long long)ch * pa.HP * pa.H;
-    const int P = pa.D - ch * pa.HP < pa.HP ? pa.D - ch * pa.HP : pa.HP;
-    if (pa.HP == 64)
-      build_slots_kernel<64><<<1, 256, 0, st>>>(tv, w, w, pa.H, P);
-    else
-      build_slots_kernel<32><<<1, 256, 0, st>>>(tv, w, w, pa.H, P);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  const size_t cb = tables_layout(bh, at);
+  const SlotTablesView tv = tables_view(tables, bh);
+  if (bh == 64)
+    build_slots_kernel<64><<<ndc * nqc, 256, 0, st>>>(tv, pa.sw, pa.sw, pa.H, pa.D, pa.H, nqc, cb);
+  else
+    build_slots_kernel<32><<<ndc * nqc, 256, 0, st>>>(tv, pa.sw, pa.sw, pa.H, pa.D, pa.H, nqc, cb);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_sensory_bwd_sparse(const SensBwdArgs& a, const SensBwdPlan& p, const void* tables,
-                                      cudaStream_t st) {
+                                      float* dxpart, cudaStream_t st) {
   if (a.rows <= 0) return cudaSuccess;
-  if (a.HP != 32 && a.HP != 64) return cudaErrorInvalidValue;
   long long rps = (a.rows + p.nsplit - 1) / p.nsplit;
   rps = (rps + kSensRows - 1) / kSensRows * kSensRows;
+  const int bh = sens_bh(a.HP);
   size_t at[7];
-  const size_t cb = tables_layout(a.HP, at);
-  const SlotTablesView tv = tables_view(const_cast<void*>(tables), a.HP);
+  const size_t cb = tables_layout(bh, at);
+  const SlotTablesView tv = tables_view(const_cast<void*>(tables), bh);
   const int S = 4 * neuron_stride4(kSensRows);
-  const size_t smem = ((size_t)4 * a.HP * S + (size_t)2 * kSensRows * (a.HP + 4)) * sizeof(float);
-  const dim3 grid(p.ndc, p.nsplit);
+  const size_t smem = ((size_t)4 * bh * S + (size_t)2 * kSensRows * (bh + 4)) * sizeof(float);
+  const dim3 grid(p.ndc * p.nqc, p.nsplit);
   cudaError_t e;
-  if (a.HP == 64) {
+  if (bh == 64) {
     e = cudaFuncSetAttribute(sens_bwd_sparse<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    sens_bwd_sparse<64><<<grid, side_nt(64, 0), smem, st>>>(a, tv, cb, rps);
+    sens_bwd_sparse<64><<<grid, side_nt(64, 0), smem, st>>>(a, tv, cb, rps, p.nqc, dxpart);
   } else {
     e = cudaFuncSetAttribute(sens_bwd_sparse<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    sens_bwd_sparse<32><<<grid, side_nt(32, 0), smem, st>>>(a, tv, cb, rps);
+    sens_bwd_sparse<32><<<grid, side_nt(32, 0), smem, st>>>(a, tv, cb, rps, p.nqc, dxpart);
   }
   return cudaGetLastError();
 }
@@ -949,9 +984,9 @@ cudaError_t launch_build_slots(const PackArgs& pa, void* tables, cudaStream_t st
   if (pa.HP > 64) return launch_build_csp(pa, tables, st);
   const SlotTablesView tv = tables_view(tables, pa.HP);
   if (pa.HP == 64)
-    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H, pa.H);
+    build_slots_kernel<64><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H, pa.H, pa.H, 1, 0);
   else
-    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H, pa.H);
+    build_slots_kernel<32><<<1, 256, 0, st>>>(tv, pa.w_pos, pa.w_erev, pa.H, pa.H, pa.H, 1, 0);
   return cudaGetLastError();
 }
 

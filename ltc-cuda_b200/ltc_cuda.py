@@ -201,7 +201,7 @@ class skip_zero_synapses:
 
     ``sensory=True`` (with ``on``) also skips the sensory synapses whose
     ``sensory_w_pos`` is zero in the sensory backward (``LTC_FLAG_SKIP_ZERO_SENSORY``,
-    H <= 64): the four sensory gradients are then zero at those positions -- again only
+    wherever the recurrent synapses are skipped: H <= 64 or 128 < H <= 512): the four sensory gradients are then zero at those positions -- again only
     for callers that discard them, as ``sensory_w_pos = softplus(w) * mask`` does.
     Check the pattern with :func:`skip_zero_sensory_fits` first."""
 
@@ -267,19 +267,18 @@ def skip_zero_synapses_fits(mask: torch.Tensor) -> bool:
 
 def skip_zero_sensory_fits(smask: torch.Tensor) -> bool:
     """True when the (D, H) sensory pattern fits the sensory backward's skipping kernel:
-    H <= 64 and, for H > 32, at most 48 nonzero synapses per input and per column
-    inside every chunk of 64 consecutive inputs."""
+    any pattern for H <= 32; otherwise at most 48 nonzero synapses per input and per
+    column inside every 64 x 64 block (64 consecutive inputs x 64 consecutive columns)."""
     D, H = smask.shape
-    if H > 64:
-        return False
     if H <= 32:
         return True
     nz = (smask != 0)
     for d0 in range(0, D, 64):
-        blk = nz[d0:d0 + 64]
-        if int(blk.sum(1).max().item()) > SKIP_MAX_SYNAPSES_PER_NEURON or \
-                int(blk.sum(0).max().item()) > SKIP_MAX_SYNAPSES_PER_NEURON:
-            return False
+        for q0 in range(0, H, 64):
+            blk = nz[d0:d0 + 64, q0:q0 + 64]
+            if int(blk.sum(1).max().item()) > SKIP_MAX_SYNAPSES_PER_NEURON or \
+                    int(blk.sum(0).max().item()) > SKIP_MAX_SYNAPSES_PER_NEURON:
+                return False
     return True
 
 

@@ -35,4 +35,7 @@ def test_sensory_capacity_check():
     # column 5 in chunk 64..127: every input's band covers it except where removed
     assert ltc_cuda.skip_zero_sensory_fits(col) == (int(col[64:128, 5].sum()) <= 48)
     assert ltc_cuda.skip_zero_sensory_fits(torch.ones(300, 32))   # H <= 32: any pattern
-    assert not ltc_cuda.skip_zero_sensory_fits(torch.ones(8, 65))  # H > 64: not honoured
+    wide = (((torch.arange(512)[None, :] - torch.arange(300)[:, None]) % 64) < 40).float()
+    assert ltc_cuda.skip_zero_sensory_fits(wide)                   # H > 64: per 64 x 64 block
+    wide[7, 100:164] = 1.0                                          # 64 in one block row
+    assert not ltc_cuda.skip_zero_sensory_fits(wide)

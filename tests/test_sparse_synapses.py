@@ -278,11 +278,13 @@ def _check_sensory(inp, U, gout, gh, ctx):
 
 
 @pytest.mark.parametrize("D,H,sdens,B,T", [(128, 64, 0.5, 9, 70), (40, 64, 0.3, 5, 20), (100, 48, 0.5, 3, 33),
-                                           (70, 32, 1.0, 4, 40), (16, 17, 0.5, 6, 9)])
+                                           (70, 32, 1.0, 4, 40), (16, 17, 0.5, 6, 9), (100, 160, 0.3, 5, 14),
+                                           (70, 300, 0.3, 6, 11), (130, 512, 0.3, 3, 9)])
 def test_sensory_backward_vs_oracle(D, H, sdens, B, T):
     """Ragged input chunks (D not a multiple of 64), rows not a multiple of the tile,
-    H <= 32 (any pattern) and a dense sensory mask at H = 32."""
-    p = synth.make_params(D, H, 0.5, sdens, seed=D + H)
+    H <= 32 (any pattern), a dense sensory mask at H = 32, and H > 128 (several column
+    blocks, dx partials summed in the finish kernel)."""
+    p = synth.make_params(D, H, 0.5 if H <= 64 else 0.2, sdens, seed=D + H)
     g = torch.Generator().manual_seed(D * H)
     x = torch.randn(B, T, D, generator=g)
     inp = {k: v.detach() for k, v in orc.module_preamble(p, x, 1 / 30, 3).items()}
