@@ -68,8 +68,8 @@ typedef struct {
  * (no counterpart in the reference, csrc/ltc_kernels.cu:675-950 visits all D*H).
  * Like the recurrent case, the caller declares the sensory_w_pos gradient unused at
  * those positions (true for softplus(w) * mask); the four sensory gradients are
- * written as zero there.  Honoured together with LTC_FLAG_SKIP_ZERO_SYNAPSES where
- * the recurrent synapses are skipped (H <= 64, 128 < H <= 512).  Capacity (H > 32):
+ * written as zero there.  Honoured together with LTC_FLAG_SKIP_ZERO_SYNAPSES, for
+ * any H, unless LTC_FLAG_FORCE_WIDE is set.  Capacity (H > 32):
  * within each block of 64 consecutive inputs x 64 consecutive columns every input
  * may feed at most 48 nonzero synapses and every column receive at most 48; beyond
  * it the outputs are NaN. */

@@ -154,7 +154,10 @@ int make_layout(const LtcDims* d, Layout* L, DeviceInfo* di) {
   L->skip_sens = (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) && !(d->flags & LTC_FLAG_FORCE_WIDE) &&
                  sens_sparse_fits(d->D);
   L->sp = plan_sensory_bwd(L->rows, d->D, L->rp.HP, di->sms);
-  L->skip_sens_bwd = (d->flags & LTC_FLAG_SKIP_ZERO_SENSORY) && L->rp.sparse && L->rp.tanh_space;
+  // the sparse sensory backward works in tanh space: it needs the recurrent backward's
+  // per-column adjoint sums, which every path but the forced wide one provides
+  L->skip_sens_bwd = (d->flags & LTC_FLAG_SKIP_ZERO_SENSORY) && (d->flags & LTC_FLAG_SKIP_ZERO_SYNAPSES) &&
+                     L->rp.tanh_space;
   if (L->skip_sens_bwd) plan_sensory_bwd_sparse(L->sp, L->rows, d->D, d->H, L->rp.HP, di->sms);
   const size_t tu = (size_t)d->T * d->ode_unfolds;
   L->lean = (d->flags & LTC_FLAG_LEAN_SAVE) != 0;

@@ -201,7 +201,7 @@ class skip_zero_synapses:
 
     ``sensory=True`` (with ``on``) also skips the sensory synapses whose
     ``sensory_w_pos`` is zero in the sensory backward (``LTC_FLAG_SKIP_ZERO_SENSORY``,
-    wherever the recurrent synapses are skipped: H <= 64 or 128 < H <= 512): the four sensory gradients are then zero at those positions -- again only
+    any H): the four sensory gradients are then zero at those positions -- again only
     for callers that discard them, as ``sensory_w_pos = softplus(w) * mask`` does.
     Check the pattern with :func:`skip_zero_sensory_fits` first."""
 
