@@ -858,6 +858,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
   }
 }
 
+
 template <typename K, typename Args>
 cudaError_t launch_plain(K kernel, const Args& a, const SlotTablesView& tv, int grid, int threads, size_t smem,
                          cudaStream_t st) {
