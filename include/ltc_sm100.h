@@ -244,6 +244,19 @@ int64_t ltc_launch_count(void);
  * Returns -1 on a CUDA error. */
 int ltc_wait_timeouts(void);
 
+/* Checked build (no counterpart in the reference).  libltc_sm100_checked.so is the
+ * same library compiled with -DLTC_CHECKED: the kernels test the indices of their
+ * table-driven gathers, shared-memory slabs and output writes, and an index out of
+ * its bound is counted and its access skipped instead of faulting the GPU.
+ * ltc_checked_build() is the number of source files whose kernels carry checks in
+ * that build, 0 in the normal one;
+ * ltc_check_errors() synchronises the device, returns the number of failed checks
+ * since the last call and the id of the first failing site (0 if none; the site ids
+ * are the LTC_CHECK call sites in the sources), and resets them.  Returns 0, or -1
+ * on a CUDA error. */
+int ltc_checked_build(void);
+int ltc_check_errors(int* count, int* first_site);
+
 /* Last error message of the calling thread ("" if none). */
 const char* ltc_last_error(void);
 

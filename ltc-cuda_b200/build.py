@@ -67,6 +67,10 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--out", default=LIB, help="output path (variant builds for tuning)")
     ap.add_argument("-D", dest="defines", action="append", default=[], help="extra preprocessor define")
+    ap.add_argument("--checked", action="store_true",
+                    help="also build libltc_sm100_checked.so (-DLTC_CHECKED: bounds-checked indices, for tests)")
     a = ap.parse_args()
     print(build(force=a.force or a.verbose_ptxas, verbose_ptxas=a.verbose_ptxas, out=os.path.abspath(a.out),
                 defines=a.defines))
+    if a.checked:
+        print(build(force=True, out=os.path.join(HERE, "libltc_sm100_checked.so"), defines=["LTC_CHECKED"]))

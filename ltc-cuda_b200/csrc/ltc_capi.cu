@@ -16,6 +16,15 @@
 #include "../../include/ltc_sm100.h"
 #include "ltc_internal.h"
 
+namespace ltc {
+// readers of the checked build's per-file error words (empty in the normal build)
+std::vector<int (*)(int*, int*)>& check_readers() {
+  static std::vector<int (*)(int*, int*)> v;
+  return v;
+}
+void register_check_reader(int (*reader)(int*, int*)) { check_readers().push_back(reader); }
+}  // namespace ltc
+
 using namespace ltc;
 
 namespace {
@@ -365,6 +374,18 @@ int ltc_preamble_backward(int64_t rows, int32_t D, const float* x, const float* 
   }
   if (e != cudaSuccess) return cuda_fail(e, "preamble_bwd");
   g_last_error.clear();
+  return 0;
+}
+
+int ltc_checked_build(void) { return (int)ltc::check_readers().size(); }
+
+int ltc_check_errors(int* count, int* first_site) {
+  if (!count || !first_site) return fail("ltc_check_errors: NULL output");
+  *count = 0;
+  *first_site = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  for (auto r : ltc::check_readers())
+    if (r(count, first_site) != 0) return -1;
   return 0;
 }
 

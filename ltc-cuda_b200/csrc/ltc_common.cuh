@@ -21,6 +21,45 @@
 
 namespace ltc {
 
+// ---- checked build (-DLTC_CHECKED) ---------------------------------------------
+// LTC_CHECK(cond, site) records an index that breaks its bound instead of trapping:
+// the failing count and the first failing site go into a per-file device word pair,
+// which the host gathers with ltc_check_errors() after a sync.  The caller of the
+// check skips the access itself (LTC_CHECKED_SKIP).  In the normal build every check
+// compiles to nothing.
+#ifdef LTC_CHECKED
+void register_check_reader(int (*reader)(int* count, int* site));
+static __device__ int g_ltc_check_count = 0;
+static __device__ int g_ltc_check_site = 0;
+__device__ __noinline__ static void ltc_check_fail(int site) {
+  atomicAdd(&g_ltc_check_count, 1);
+  atomicCAS(&g_ltc_check_site, 0, site);
+}
+#define LTC_CHECK(cond, site) \
+  do {                        \
+    if (!(cond)) ::ltc::ltc_check_fail(site); \
+  } while (0)
+// evaluates to true when the access must be skipped
+#define LTC_CHECKED_SKIP(cond, site) (!(cond) ? (::ltc::ltc_check_fail(site), true) : false)
+static int ltc_check_read(int* count, int* site) {
+  int c = 0, s = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&c, g_ltc_check_count, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&s, g_ltc_check_site, sizeof(int));
+  const int zero = 0;
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_ltc_check_count, &zero, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_ltc_check_site, &zero, sizeof(int));
+  *count += c;
+  if (!*site) *site = s;
+  return (int)e;
+}
+static struct LtcCheckRegistration {
+  LtcCheckRegistration() { register_check_reader(&ltc_check_read); }
+} s_ltc_check_registration;
+#else
+#define LTC_CHECK(cond, site) ((void)0)
+#define LTC_CHECKED_SKIP(cond, site) false
+#endif
+
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

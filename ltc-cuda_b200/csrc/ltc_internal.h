@@ -1,11 +1,13 @@
 // Internal launch interfaces shared by the kernel translation units and the C-ABI layer.
 #pragma once
+#include <vector>
 
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
 namespace ltc {
+std::vector<int (*)(int*, int*)>& check_readers();
 
 // ---- parameter packing --------------------------------------------------
 struct PackArgs {

@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
         }
         LR::template run<2>(acc, lane);
         const int s = blk * kSB + osmp;
+        LTC_CHECK(s < ns && q >= 0 && q < HP, 401);
         const float v = vc[s * LDV + q];
         const float wn = acc[0][0] + snb[s * LDV + q];
         const float wd = acc[1][0] + sdb[s * LDV + q];
@@ -439,6 +440,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
     const int m = NTU - 1;
     for (int blk = 0; blk < nblk; ++blk) {
       const int s = blk * kSB + osmp;
+      LTC_CHECK(s < ns && p >= 0 && p < HP, 402);
       if (pvalid && s < nvalid) {
         const long long bs = b0 + s;
         float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
@@ -516,6 +518,7 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
       }
       LR::template run<1>(acc, lane);
       const int s = blk * kSB + osmp;
+      LTC_CHECK(s < ns && p >= 0 && p < HP, 403);
       if (writer && !(pvalid && s < nvalid) && n > 0) send_zero(an_m, ad_m, s);
       if (pvalid && writer && s < nvalid) {
         const int idx = s * LDV + p;

@@ -249,7 +249,9 @@ __global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables t
     const int q = nb + c;
     float se = 0.f, sp = 0.f;
     for (int e = coff[c] + lane; e < coff[c + 1]; e += 32) {
-      const int p = tb.fent[r * kFCap + e];
+      if (LTC_CHECKED_SKIP(e >= 0 && e < kFCap, 201)) continue;
+      int p = tb.fent[r * kFCap + e];
+      if (LTC_CHECKED_SKIP(p >= 0 && p < HP, 202)) p = 0;
       float4 k = a.pack[(long long)p * HP + q];
       k.z *= 0.5f;
       k.w *= 0.5f;
@@ -348,7 +350,7 @@ __global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables t
             an1 += __shfl_xor_sync(0xffffffffu, an1, off);
             ad1 += __shfl_xor_sync(0xffffffffu, ad1, off);
           }
-          if (owner) {
+          if (owner && !LTC_CHECKED_SKIP(b0 + s < B && b0 + s < BP && q < HP, 203)) {
             const long long bs = b0 + s;
             const float v = vs[q * kFS + (s - g * kFS)];
             const float num = (nq.x * v + nq.w) + ((cw[c] + an1) + snv);
@@ -488,7 +490,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
   // the lane's synapse constants (-sigma/2, sigma*mu/2, w_pos, w_erev) and columns;
   // padding slots get zero constants and read column 0
   for (int j = 0; j < kBK; ++j) {
-    const uint16_t q = active ? tb.bidx[(size_t)r * kBK * kNT + j * kNT + tid] : (uint16_t)0xFFFF;
+    uint16_t q = active ? tb.bidx[(size_t)r * kBK * kNT + j * kNT + tid] : (uint16_t)0xFFFF;
+    if (q != 0xFFFF && LTC_CHECKED_SKIP(q < HP, 211)) q = 0xFFFF;
     float4 k = make_float4(0.f, 0.f, 0.f, 0.f);
     if (q != 0xFFFF) {
       k = a.pack[(long long)prow(j < K1w ? 0 : 1) * HP + q];
@@ -617,7 +620,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
           f.template pass<decltype(K1)::value, decltype(K2)::value>(cst, qix, an_b, ad_b, vr, acc, tid);
         });
         LR::template run<1>(acc, lane);
-        if (active) dvb[(2 * c + own / kSB) * kCS + blk * kSB + own % kSB] = acc[0][0];
+        if (active && !LTC_CHECKED_SKIP(2 * c + own / kSB < NEUR, 212))
+          dvb[(2 * c + own / kSB) * kCS + blk * kSB + own % kSB] = acc[0][0];
       }
       __syncthreads();  // adjoint buffers free: the next chunk streams in behind the tails
       if (ch + 1 < nch) stage(ch + 1, (ch + 1) & 1);
@@ -666,7 +670,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
 #pragma unroll
     for (int j = 0; j < kBK; ++j) {
       const uint16_t q = tb.bidx[(size_t)r * kBK * kNT + j * kNT + tid];
-      if (q == 0xFFFF) continue;
+      if (q == 0xFFFF || LTC_CHECKED_SKIP(q < HP, 213)) continue;
       const long long idx = (long long)prow(j < K1w ? 0 : 1) * HP + q;
       if (a.accumulate) {
         part[idx] += f.Gwe[j];

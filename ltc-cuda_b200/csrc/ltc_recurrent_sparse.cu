@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(256) build_slots_kernel(SlotTablesView tv, con
       const int cb = ccount[s][n][bb];
       pos += min(cb, k) + ((bb < b && cb > k) ? 1 : 0);
     }
-    lst[s][n][pos] = (unsigned char)o;
+    if (!LTC_CHECKED_SKIP(pos < HP, 101)) lst[s][n][pos] = (unsigned char)o;
   }
   __syncthreads();
   // ... then every thread fills slots of both tables in parallel
@@ -346,7 +346,8 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int base = (tid * 2 + r) * KM + j;
-      const int ix = tv.fidx[base];  // presynaptic neuron; the constants come from the dense pack
+      int ix = tv.fidx[base];  // presynaptic neuron; the constants come from the dense pack
+      if (LTC_CHECKED_SKIP(ix < HP && tv.fneu[2 * c + r] >= 0 && tv.fneu[2 * c + r] < HP, 102)) ix = -1;
       float4 pk = ix < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : a.pack[(long long)ix * HP + tv.fneu[2 * c + r]];
       pk.z *= 0.5f;
       pk.w *= 0.5f;
@@ -407,13 +408,14 @@ __global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a
         });
         LR::template run<2>(acc, lane);
         const int s = blk * kSB + osmp;
+        LTC_CHECK(s < S && q >= 0 && q < HP, 103);
         const float v = vc[q * S + s];
         const float wn = acc[0][0] + snb[s * LDV + q];
         const float wd = acc[1][0] + sdb[s * LDV + q];
         const float num = (cm * v + glvl) + wn;
         const float rr = rcp_approx((cmgl + wd) + a.eps);
         const float vnew = overflow ? __int_as_float(0x7fc00000) : num * rr;
-        if (writer && qvalid && s < nvalid) {
+        if (writer && qvalid && s < nvalid && !LTC_CHECKED_SKIP(b0 + s < B && q < H, 104)) {
           vn[q * S + s] = vnew;
           const long long bs = b0 + s;
           if (a.V) {
@@ -527,7 +529,8 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int base = (tid * 2 + r) * KM + j;
-      const int ix = tv.bidx[base];  // postsynaptic neuron; the constants come from the dense pack
+      int ix = tv.bidx[base];  // postsynaptic neuron; the constants come from the dense pack
+      if (LTC_CHECKED_SKIP(ix < HP && rowA >= 0 && rowA < HP && rowB >= 0 && rowB < HP, 111)) ix = -1;
       float4 pk = ix < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : a.pack[(long long)(r ? rowB : rowA) * HP + ix];
       pk.x = -pk.x;  // negated half-scale constants: the gate argument is -z/2
       pk.y = -pk.y;
@@ -649,7 +652,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
       });
       LR::template run<1>(acc, lane);
       const int s = blk * kSB + osmp;
-      if (pvalid && writer && s < nvalid) {
+      if (pvalid && writer && s < nvalid && !LTC_CHECKED_SKIP(s < ns && p < HP && b0 + s < B, 112)) {
         const int idx = s * LDV + p;
         float gval = fmaf(-2.0f, acc[0][0], DIR[idx]);
         const long long bs = b0 + s;
@@ -684,7 +687,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1) rec_bwd_sparse(RecBwdArgs a
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int qi = tv.bidx[(tid * 2 + r) * KM + j];
-      if (qi < 0) continue;
+      if (qi < 0 || LTC_CHECKED_SKIP(qi < HP && row >= 0 && row < HP, 113)) continue;
       const int idx = row * HP + qi;
       const float v0 = f.Gwe[r][j].x + f.Gwe[r][j].y, v1 = f.Gwp[r][j].x + f.Gwp[r][j].y;
       const float v2 = f.Gdz[r][j].x + f.Gdz[r][j].y, v3 = f.Gdzv[r][j].x + f.Gdzv[r][j].y;
@@ -772,7 +775,8 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int base = (tid * 2 + r) * KM + j;
-      const int ix = tv.bidx[base];  // column q
+      int ix = tv.bidx[base];  // column q
+      if (LTC_CHECKED_SKIP(ix < HP && rowA >= 0 && rowA < HP && rowB >= 0 && rowB < HP, 121)) ix = -1;
       const int d = d0 + (r ? rowB : rowA);
       float4 pk = (ix < 0 || d >= D) ? make_float4(0.f, 0.f, 0.f, 0.f) : a.spack[(long long)d * a.HP + q0 + ix];
       pk.x = -pk.x;  // gate argument -z/2
@@ -834,6 +838,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
       if (writer && pvalid && s < nr) {
         const float v = -2.0f * acc[0][0] + bad;  // sl holds -sigma/2
         const long long o = (rt + s) * D + d0 + p;
+        if (LTC_CHECKED_SKIP(rt + s < a.rows && d0 + p < D, 122)) continue;
         if (nqc == 1) a.dx[o] = v;
         else dxpart[(long long)(chunk % nqc) * a.rows * D + o] = v;
       }
@@ -848,7 +853,7 @@ __global__ void __launch_bounds__(side_nt(HP, 0), 1)
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       const int qi = tv.bidx[(tid * 2 + r) * KM + j];
-      if (qi < 0 || d >= D) continue;
+      if (qi < 0 || d >= D || LTC_CHECKED_SKIP(qi < HP && q0 + qi < a.HP, 123)) continue;
       const long long idx = (long long)d * a.HP + q0 + qi;
       part[idx] = -0.25f * (f.Gwe[r][j].x + f.Gwe[r][j].y);
       part[slab + idx] = -0.25f * (f.Gwp[r][j].x + f.Gwp[r][j].y);

@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(256) build_sens_kernel(SensTablesView tv, cons
     const unsigned m = __ballot_sync(0xffffffffu, on);
     if (on) {
       const int pos = base + __popc(m & ((1u << lane) - 1u));
+      LTC_CHECK(pos < D, 301);
       const float4 k = spack[(long long)d * HP + q];
       tv.idx[(long long)q * D + pos] = d;
       tv.cst[(long long)q * D + pos] = k;
@@ -179,7 +180,9 @@ __global__ void __launch_bounds__(kNT, 1) sens_fwd_sparse(SensFwdArgs a, SensTab
             const int k = j * 32 + lane;
             if (k < m) {
               lcs[k] = lc[base + k];
-              lis[k] = li[base + k] * TR;
+              int d = li[base + k];
+              if (LTC_CHECKED_SKIP(d >= 0 && d < D, 302)) d = 0;
+              lis[k] = d * TR;
             }
           }
           __syncwarp();
