@@ -320,6 +320,18 @@ def rec_synapses(model, cfg, rows) -> int:
     return cfg.H * cfg.H
 
 
+def sens_synapses(model, cfg, rows):
+    """Sensory synapses per (b,t) the sensory forward and backward visit: the nonzero
+    ones where the module lets the solver skip masked synapses (the forward whenever it
+    skips the recurrent ones, the backward when its sensory mask fits), else D*H."""
+    import ltc_layer
+    full = cfg.D * cfg.H
+    if not (getattr(model, "skip_zero_synapses", False) and model._skip_fits() and rows >= ltc_layer.SKIP_MIN_ROWS):
+        return full, full
+    nnz = int(model.sensory_sparsity_mask.count_nonzero().item())
+    return nnz, (nnz if model._skip_sensory_fits() else full)
+
+
 def our_parity(cfg, p, dev, skip_zero=True):
     """Parity of this build's module on a slice of the timed configuration, checked
     before the timed region against the reference TorchScript path (or, where the
@@ -592,10 +604,11 @@ def main():
     # recurrent synapses the kernels visit: the nonzero ones when the module lets the
     # solver skip masked synapses (H <= 64 or 128 < H <= 512), else all H*H
     rec_syn = rec_synapses(model, cfg, Bl * cfg.T)
+    sens_syn = sens_synapses(model, cfg, Bl * cfg.T)
     visits = {"recurrent_fwd": Bl * cfg.T * cfg.U * rec_syn,
               "recurrent_bwd": Bl * cfg.T * cfg.U * rec_syn,
-              "sensory_fwd": Bl * cfg.T * cfg.D * cfg.H,
-              "sensory_bwd": Bl * cfg.T * cfg.D * cfg.H}
+              "sensory_fwd": Bl * cfg.T * sens_syn[0],
+              "sensory_bwd": Bl * cfg.T * sens_syn[1]}
     # Work per step of each kernel kind.  Memory-lean training runs the forward
     # kernels twice per step (the forward, then the recompute inside the backward,
     # once per segment), so their work per step doubles; every figure below is
@@ -617,7 +630,7 @@ def main():
     kernels = {k: {"ms_total": round(v[0], 3), "launches": v[1], "share": round(v[0] / max(1e-9, sum(
         t for t, _ in ktimes.values())), 4)} for k, v in ktimes.items()}
     # whole-step ceiling with the survey's counting convention (4 MUFU per fwd+bwd synapse visit)
-    S = cfg.D * cfg.H + cfg.U * rec_syn  # nonzero recurrent synapses when they are skipped
+    S = sens_syn[0] + cfg.U * rec_syn  # nonzero synapses when they are skipped
     t_roof = cfg.B * cfg.T * S * 4 / (16 * sms * f_mhz * 1e6 * world)
     # recurrent kernels alone, same convention (the H=128 north-star figure)
     per_step = lambda k: ktimes[k][0] / args.steps / 1e3  # seconds of kernel kind k per step
@@ -637,7 +650,8 @@ def main():
                    "l2": "256 MB flush write between steps (inside the timed region)",
                    "cuda_graph": use_graph if graph_note is None else graph_note,
                    "saved_state": "step boundaries, unfolds recomputed (lean)" if args.lean else "every unfold",
-                   "recurrent_synapses_visited": rec_syn, "recurrent_synapses_dense": cfg.H * cfg.H},
+                   "recurrent_synapses_visited": rec_syn, "recurrent_synapses_dense": cfg.H * cfg.H,
+                   "sensory_synapses_visited": list(sens_syn), "sensory_synapses_dense": cfg.D * cfg.H},
         "e2e": e2e,
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "Gsynapse-visits/s",
                      "frac": achieved / peak, "ms_per_launch": ms_per_launch,
