@@ -7,7 +7,7 @@
 // declares those gradients unused; these kernels then visit only the nonzero
 // synapses and the finish kernel writes zeros at the skipped positions.
 //
-// Layout.  TPC lanes (8 in the backward, 16 in the forward) share a PAIR of
+// Layout.  TPC = 8 lanes share a PAIR of
 // neurons (rows in the backward, columns in the forward): the c-th heaviest and
 // the c-th lightest by nonzero count, so every pair carries a similar total.
 // Each lane holds up to KM synapses of each neuron, taken from the neuron's
@@ -42,13 +42,13 @@ namespace ltc {
 namespace {
 
 constexpr int kSB = 4;   // samples per block (one float4 of a neuron-major vector)
-// lanes per neuron pair and slots per neuron and lane: the forward (side 1) uses
-// 16 lanes per pair (512 threads at HP = 64; its registers allow it, and the
-// MUFU-bound pass wants the warps), the backward (side 0) 8 lanes per pair
-// (256 threads; 16 registers per slot).  Capacity is 48 synapses per neuron at
-// HP = 64 and 32 (every mask) at HP = 32 either way.
+// lanes per neuron pair and slots per neuron and lane, forward (side 1) and backward
+// (side 0): 8 lanes per pair (256 threads at HP = 64; one reduced item per lane in
+// the tails; 16 lanes per pair in the forward measured the same at c3 and 3% slower
+// at 4 samples per CTA).  Capacity is 48 synapses per neuron at HP = 64 and 32 (every
+// mask) at HP = 32.
 constexpr int kCap64 = 48;
-__host__ __device__ constexpr int side_tpc(int side) { return side ? 16 : 8; }
+__host__ __device__ constexpr int side_tpc(int) { return 8; }
 __host__ __device__ constexpr int side_km(int HP, int side) { return (HP == 64 ? kCap64 : 32) / side_tpc(side); }
 __host__ __device__ constexpr int side_nt(int HP, int side) { return HP / 2 * side_tpc(side); }
 
