@@ -320,7 +320,7 @@ struct SparseFwd {
 };
 
 template <int HP>
-__global__ void __launch_bounds__(side_nt(HP, 1), 1) rec_fwd_sparse(RecFwdArgs a, SlotTablesView tv) {
+__global__ void __launch_bounds__(side_nt(HP, 1), 2) rec_fwd_sparse(RecFwdArgs a, SlotTablesView tv) {
   using F = SparseFwd<HP>;
   constexpr int NT = F::NT, KM = F::KM, LDV = F::LDV, TPC = F::TPC;
   using LR = LaneReduce<TPC, 2 * kSB>;
@@ -902,13 +902,20 @@ void plan_sparse(RecPlan& p, int B, int num_sms) {
   if (per < 1) per = 1;
   const int ns = per * kSB;
   const int S = 4 * neuron_stride4(ns);
+  // the forward (128 registers, small shared memory) runs two CTAs per SM: its groups
+  // are planned over twice the SMs, so two groups overlap their per-unfold latency
+  const int per_f = (int)((blocks + 2LL * num_sms - 1) / (2LL * num_sms));
+  const int ns_f = per_f * kSB;
+  const int S_f = 4 * neuron_stride4(ns_f);
   p.sparse = true;
-  p.ns_fwd = p.ns_bwd = ns;
-  p.grid_fwd = p.grid_bwd = (B + ns - 1) / ns;
+  p.ns_fwd = ns_f;
+  p.ns_bwd = ns;
+  p.grid_fwd = (B + ns_f - 1) / ns_f;
+  p.grid_bwd = (B + ns - 1) / ns;
   p.threads_fwd = side_nt(HP, 1);
   p.threads_bwd = side_nt(HP, 0);
   p.slots_bwd = p.grid_bwd;
-  p.smem_fwd = ((size_t)2 * HP * S + 4 * (size_t)ns * LDV) * sizeof(float);
+  p.smem_fwd = ((size_t)2 * HP * S_f + 4 * (size_t)ns_f * LDV) * sizeof(float);
   p.smem_bwd = bwd_bytes(ns);
   p.tanh_space = true;
 }
