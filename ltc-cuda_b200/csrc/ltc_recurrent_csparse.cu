@@ -219,6 +219,11 @@ __global__ void __launch_bounds__(kNT) build_csp_kernel(CspTables tb, const floa
   }
 }
 
+// Saved state.  On this path V and R are stored neuron-major per unfold,
+// V[n][q][b] (n in [0, T*U], the last slice the final state) and R[n][q][b]: the
+// forward's owner lanes are consecutive samples of one neuron, so its stores and the
+// backward's staging reads are contiguous.  Only these two kernels read or write it.
+
 // ---- forward --------------------------------------------------------------------
 // scratch: vstate [2][HP][BP] neuron-major (BP = planned sample capacity)
 template <int NEUR>
@@ -358,8 +363,8 @@ __global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables t
             const float vnew = bad ? __int_as_float(0x7fc00000) : num * rr;
             vn[(long long)q * BP + bs] = vnew;
             if (a.V) {
-              a.V[(n * B + bs) * H + q] = v;
-              a.R[(n * B + bs) * H + q] = rr;
+              a.V[(n * H + q) * B + bs] = v;  // neuron-major saved state (this path's own layout)
+              a.R[(n * H + q) * B + bs] = rr;
             }
             if (u == U - 1 && a.out) a.out[row * H + q] = vnew;
           }
@@ -377,7 +382,7 @@ __global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables t
     const long long bs = b0 + s;
     const float v = vc[(long long)q * BP + bs];
     if (a.hT) a.hT[bs * H + q] = v;
-    if (a.V) a.V[((long long)T * U * B + bs) * H + q] = v;
+    if (a.V) a.V[((long long)T * U * H + q) * B + bs] = v;
   }
   cluster.sync();  // no CTA leaves while a peer may still read its states
 }
@@ -544,8 +549,8 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
           float gval = a.gout[bs * a.go_sb + (long long)(T - 1) * a.go_st + (long long)p * a.go_sh];
           if (a.gstate) gval += a.gstate[bs * H + p];
           const long long m = NTU - 1;
-          prep(rsel, NTU - 1, bs, gval, true, a.V[(m * B + bs) * H + p], a.V[((m + 1) * B + bs) * H + p],
-               a.R[(m * B + bs) * H + p], 0.f, 0.f);
+          prep(rsel, NTU - 1, bs, gval, true, a.V[(m * H + p) * B + bs], a.V[((m + 1) * H + p) * B + bs],
+               a.R[(m * H + p) * B + bs], 0.f, 0.f);
         } else {
           for (int par = 0; par < 2; ++par) {
             ANg[par * SV + (long long)p * BP + bs] = 0.f;
@@ -581,9 +586,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
         const bool ok = sc + sl < nvalid && row < H && (fld == 0 || fld >= 3 || !last);
         const float* src;
         switch (fld) {
-          case 0: src = a.V + ((long long)n * B + bs) * H + row; break;
-          case 1: src = a.V + ((long long)(n - 1) * B + bs) * H + row; break;
-          case 2: src = a.R + ((long long)(n - 1) * B + bs) * H + row; break;
+          case 0: src = a.V + ((long long)n * H + row) * B + bs; break;
+          case 1: src = a.V + ((long long)(n - 1) * H + row) * B + bs; break;
+          case 2: src = a.R + ((long long)(n - 1) * H + row) * B + bs; break;
           case 3: src = DIRg + bs * HP + row; break;
           case 4: src = GSNg + bs * HP + row; break;
           default: src = GSDg + bs * HP + row; break;
