@@ -197,6 +197,26 @@ __device__ __forceinline__ void cp_async4_zfill(void* smem, const void* gmem, bo
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(valid ? 4 : 0));
 }
+// Rows 0 .. nrows-1 of H floats each (row s at src + s * src_ld) -> shared rows of
+// stride ld floats, asynchronously: 16-byte copies when both bases are 16-byte aligned
+// and H, src_ld and ld are multiples of 4 (every row then stays aligned), else 4-byte
+// copies (a caller's workspace need not be 16-byte aligned).
+__device__ __forceinline__ void stage_rows_async(float* dst, int ld, const float* src, long long src_ld,
+                                                 int nrows, int H, int tid, int nt) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+  if (aligned && ((H | ld | (int)(src_ld & 3)) & 3) == 0) {
+    const int h4 = H >> 2;
+    for (int i = tid; i < nrows * h4; i += nt) {
+      const int s = i / h4, k = i - s * h4;
+      cp_async16(dst + s * ld + 4 * k, src + s * src_ld + 4 * k);
+    }
+  } else {
+    for (int i = tid; i < nrows * H; i += nt) {
+      const int s = i / H, h = i - s * H;
+      cp_async4(dst + s * ld + h, src + s * src_ld + h);
+    }
+  }
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::); }
 

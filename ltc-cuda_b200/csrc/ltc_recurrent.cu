@@ -176,12 +176,9 @@ __global__ void __launch_bounds__(Geometry<HP, fwd_rpt<HP>(), cluster_of<HP>()>:
   auto stage_sens = [&](int t) {
     float* dn = snb2 + (t & 1) * ns * LDV;
     float* dd = sdb2 + (t & 1) * ns * LDV;
-    for (int i = tid; i < nvalid * H; i += NT) {
-      const int s = i / H, h = i % H;
-      const long long row = (long long)(b0 + s) * T + t;
-      cp_async4(dn + s * LDV + h, a.sn + row * H + h);
-      cp_async4(dd + s * LDV + h, a.sd + row * H + h);
-    }
+    const long long row0 = (long long)b0 * T + t;  // sample s's row is row0 + s * T
+    stage_rows_async(dn, LDV, a.sn + row0 * H, (long long)T * H, nvalid, H, tid, NT);
+    stage_rows_async(dd, LDV, a.sd + row0 * H, (long long)T * H, nvalid, H, tid, NT);
     cp_async_commit();
   };
   stage_sens(0);
@@ -364,12 +361,12 @@ __global__ void __launch_bounds__(Geometry<HP, bwd_rpt<HP>(), cluster_of<HP>()>:
   auto stage_v = [&](int m) {
     float* dst = VS + (m % 3) * SL;
     const float* src = a.V + ((long long)m * B + b0) * H;
-    for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
+    stage_rows_async(dst, LDV, src, H, nvalid, H, tid, NT);
   };
   auto stage_r = [&](int m) {
     float* dst = RS + (m % 2) * SL;
     const float* src = a.R + ((long long)m * B + b0) * H;
-    for (int i = tid; i < nvalid * H; i += NT) cp_async4(dst + (i / H) * LDV + (i % H), src + i);
+    stage_rows_async(dst, LDV, src, H, nvalid, H, tid, NT);
   };
   // dL/dout of step tt (strided) -> GO[tt & 1], copied in while later unfolds run;
   // a gradient broadcast over samples and steps (stride 0, e.g. a sum loss) is
