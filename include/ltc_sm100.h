@@ -55,9 +55,12 @@ typedef struct {
  * 128 < H <= 512 (64 < H <= 128 runs the dense kernels); the synapse tables are
  * rebuilt on the device at every call.  Capacity: for 32 < H <= 64 every neuron may
  * have at most 48 nonzero incoming and 48 nonzero outgoing synapses (any pattern
- * fits for H <= 32); for 128 < H <= 512 at most 128 nonzero synapses leave each
- * neuron and at most 8192 enter each block of HP/8 consecutive neurons (HP = 256
- * for H <= 256, else 512).  The library cannot
+ * fits for H <= 32); for 128 < H <= 512 (HP = 256 for H <= 256, else 512) at most
+ * 8192 nonzero synapses enter each block of HP/8 consecutive neurons, and inside
+ * each such block of rows, ranked by outgoing count and paired c-th heaviest with
+ * c-th lightest in groups of 4 pairs, 4*ceil(max ceil(heavy/8)/4) +
+ * 4*ceil(max ceil(light/8)/4) <= 32 (the rule ltc_cuda.skip_zero_synapses_fits
+ * applies; roughly 120 per row at uniform density).  The library cannot
  * report a violation without a device sync, so a call that exceeds it writes NaN
  * to its outputs and gradients; check the pattern before setting the flag.
  * The same flag makes the sensory forward visit only the sensory synapses with

@@ -11,23 +11,26 @@
 // is re-streamed per unfold except the per-neuron vectors, which go through L2
 // (global scratch, neuron-major) and are ordered by one cluster barrier per unfold.
 //
-// Forward: a warp takes one column and 32 samples (lanes).  The column's list is
-// walked in lockstep, so each synapse's constants are a shared-memory broadcast
-// and the presynaptic states v[p][lane] of the staged 32-sample slice are
-// conflict-free loads; each lane owns its (column, sample) sum, so no lane
-// reduction is needed.  A slice with <= 16 (<= 8) samples splits the list over 2
-// (4) lane parts instead of idling lanes, and combines them with shuffles.
-// Backward: 4 lanes share a row (64 rows x 4 = 256 threads at HP = 512); a lane
-// holds up to 32 of the row's synapses with their 4 gradient sums in registers for
-// the whole sequence and their constants in shared memory; samples come in chunks
-// of 8, the adjoints of all HP columns for the chunk staged neuron-major (odd
-// float4 stride) and gathered per synapse; the per-(row, sample) sum dL/dv is
-// reduced over the 4 lanes by the transposed reduction.  Rows are ranked by count
-// so a warp's 8 rows need similar slot counts, which run as compile-time constants.
+// Forward: a warp takes one column; lane = (sample quad, list part): each lane runs
+// 4 samples of a staged 32-sample slice per list entry (one float4 gather of the
+// presynaptic states, the entry's constants a shared-memory broadcast), the list is
+// split over 32 / quads parts, and a transposed shuffle reduction over the parts
+// leaves one (column, sample) sum per owner lane.
+// Backward: 8 lanes share a pair of rows (the c-th heaviest and the c-th lightest
+// by count); a lane holds up to 32 slots of the pair's synapses with their 4
+// gradient sums in registers for the whole sequence and their constants in shared
+// memory; samples come in chunks of 8, the adjoints of all HP columns for the chunk
+// staged neuron-major (odd float4 stride) and gathered per synapse; the
+// per-(row, sample) sum dL/dv is reduced over the 8 lanes by the transposed
+// reduction.  A warp's slot counts (K1, K2) run as compile-time constants.
+// The saved V / R of this path are neuron-major (see below).
 //
-// Capacity (HP = 512): at most 128 nonzero synapses per row and 8192 per block of
-// 64 columns; HP = 256: 128 per row (any column block fits).  The table builder
-// flags a violation and the kernels then write NaN to their outputs.
+// Capacity: at most 8192 nonzero synapses enter each CTA's block of HP/8 columns;
+// inside each block of HP/8 rows, with the rows ranked by count and paired c-th
+// heaviest with c-th lightest in warps of 4 pairs, a warp needs K1 + K2 <= 32 slots
+// (K1 = 4*ceil(max ceil(heavy/8) / 4), K2 likewise for the light rows).  The table
+// builder flags a violation and the kernels then write NaN to their outputs
+// (ltc_cuda.skip_zero_synapses_fits applies the same rule on the host).
 #include <cooperative_groups.h>
 
 #include <cstdint>
@@ -579,7 +582,28 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
         cp_async16(adc + q * 4 * kCS4 + 4 * k4, ADn + (long long)q * BP + b0 + sc + 4 * k4);
       }
       float* td = tdat + tbuf * 6 * NEUR * kCS;
-      for (int i = tid; i < 6 * NEUR * kCS; i += kNT) {
+      // V[n], V[n-1], R[n-1] of a full chunk are kCS contiguous samples per row (the
+      // neuron-major saved state): 16-byte copies when every row stays aligned
+      const bool vec = (B & 3) == 0 && sc + kCS <= nvalid &&
+                       ((reinterpret_cast<uintptr_t>(a.V) | reinterpret_cast<uintptr_t>(a.R)) & 15) == 0;
+      const int f0 = vec ? 3 : 0;  // first field of the per-element loop
+      if (vec) {
+        for (int i = tid; i < 3 * NEUR * (kCS / 4); i += kNT) {
+          const int fld = i / (NEUR * (kCS / 4)), rs = (i / (kCS / 4)) % NEUR, k4 = i % (kCS / 4);
+          const int row = rowof[rs];
+          float* dst = td + (fld * NEUR + rs) * kCS + 4 * k4;
+          if (row < H && (fld == 0 || !last)) {
+            const long long bs = b0 + sc + 4 * k4;
+            const float* src = fld == 0 ? a.V + ((long long)n * H + row) * B + bs
+                             : fld == 1 ? a.V + ((long long)(n - 1) * H + row) * B + bs
+                                        : a.R + ((long long)(n - 1) * H + row) * B + bs;
+            cp_async16(dst, src);
+          } else {
+            *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+      for (int i = tid + f0 * NEUR * kCS; i < 6 * NEUR * kCS; i += kNT) {
         const int fld = i / (NEUR * kCS), rs = (i / kCS) % NEUR, sl = i % kCS;
         const int row = rowof[rs];
         const long long bs = b0 + sc + sl;
