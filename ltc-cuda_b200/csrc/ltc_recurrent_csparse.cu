@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(kNTF, 1) rec_fwd_csp(RecFwdArgs a, CspTables t
 }
 
 // ---- backward -------------------------------------------------------------------
-// scratch: AN, AD [2][HP][BP] neuron-major (by unfold parity); DIR, GSN, GSD [B][HP]
+// scratch: AN, AD [2][HP][BP] neuron-major (by unfold parity); DIR, GSN, GSD [HP][B]
 struct CspBwd {
   float Gwe[kBK], Gwp[kBK], Gdz[kBK], Gdzv[kBK];
 
@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
     sums[rsel][2] = fmaf(an, nrn2[rsel].y, sums[rsel][2]);
     sums[rsel][3] += an;
     sums[rsel][4] += ad;
-    const long long o = bs * HP + p;
+    const long long o = (long long)p * B + bs;  // neuron-major, like the saved state
     GSNg[o] = first ? an : gsn_prev + an;
     GSDg[o] = first ? ad : gsd_prev + ad;
     DIRg[o] = an * nrn2[rsel].x;
@@ -582,21 +582,25 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
         cp_async16(adc + q * 4 * kCS4 + 4 * k4, ADn + (long long)q * BP + b0 + sc + 4 * k4);
       }
       float* td = tdat + tbuf * 6 * NEUR * kCS;
-      // V[n], V[n-1], R[n-1] of a full chunk are kCS contiguous samples per row (the
-      // neuron-major saved state): 16-byte copies when every row stays aligned
+      // every field of a full chunk is kCS contiguous samples per row (neuron-major
+      // saved state and scratch): 16-byte copies when every row stays aligned
       const bool vec = (B & 3) == 0 && sc + kCS <= nvalid &&
-                       ((reinterpret_cast<uintptr_t>(a.V) | reinterpret_cast<uintptr_t>(a.R)) & 15) == 0;
-      const int f0 = vec ? 3 : 0;  // first field of the per-element loop
+                       ((reinterpret_cast<uintptr_t>(a.V) | reinterpret_cast<uintptr_t>(a.R) |
+                         reinterpret_cast<uintptr_t>(DIRg)) & 15) == 0;
+      const int f0 = vec ? 6 : 0;  // first field of the per-element loop
       if (vec) {
-        for (int i = tid; i < 3 * NEUR * (kCS / 4); i += kNT) {
+        for (int i = tid; i < 6 * NEUR * (kCS / 4); i += kNT) {
           const int fld = i / (NEUR * (kCS / 4)), rs = (i / (kCS / 4)) % NEUR, k4 = i % (kCS / 4);
           const int row = rowof[rs];
           float* dst = td + (fld * NEUR + rs) * kCS + 4 * k4;
-          if (row < H && (fld == 0 || !last)) {
+          if (row < H && (fld == 0 || fld >= 3 || !last)) {
             const long long bs = b0 + sc + 4 * k4;
             const float* src = fld == 0 ? a.V + ((long long)n * H + row) * B + bs
                              : fld == 1 ? a.V + ((long long)(n - 1) * H + row) * B + bs
-                                        : a.R + ((long long)(n - 1) * H + row) * B + bs;
+                             : fld == 2 ? a.R + ((long long)(n - 1) * H + row) * B + bs
+                             : fld == 3 ? DIRg + (long long)row * B + bs
+                             : fld == 4 ? GSNg + (long long)row * B + bs
+                                        : GSDg + (long long)row * B + bs;
             cp_async16(dst, src);
           } else {
             *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -613,9 +617,9 @@ __global__ void __launch_bounds__(kNT, 1) rec_bwd_csp(RecBwdArgs a, CspTables tb
           case 0: src = a.V + ((long long)n * H + row) * B + bs; break;
           case 1: src = a.V + ((long long)(n - 1) * H + row) * B + bs; break;
           case 2: src = a.R + ((long long)(n - 1) * H + row) * B + bs; break;
-          case 3: src = DIRg + bs * HP + row; break;
-          case 4: src = GSNg + bs * HP + row; break;
-          default: src = GSDg + bs * HP + row; break;
+          case 3: src = DIRg + (long long)row * B + bs; break;
+          case 4: src = GSNg + (long long)row * B + bs; break;
+          default: src = GSDg + (long long)row * B + bs; break;
         }
         cp_async4_zfill(td + i, ok ? src : a.V, ok);
       }
